@@ -1,0 +1,465 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fused-kernel path behind tinker_b200.optimize().
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (``value``): forward latency of the 268M Llama-style decoder
+(vocab 32000, hidden 1024, 18 layers, 16/4 heads, head_dim 64, FFN 2816,
+fp16, seeded N(0, 0.02) weights) at batch 1 x seq 128, captured in a CUDA
+graph by ``optimize(cuda_graph=True)``; inputs resident in HBM, time per graph
+replay from CUDA events. With N GPUs (torchrun, one process per GPU) every rank
+runs an independent replica - the path has no collective - and ``value`` is the
+max over ranks. ``e2e`` times the same forward through the public call with
+the token ids copied from pinned host memory and the logits copied back.
+
+Also reported: ``batched`` - Qwen2.5-0.5B-shaped bf16 prefill of batch 64 x
+seq 512, the 64 sequences split into contiguous blocks of 64/N per rank
+(aggregate tokens/s); ``roofline`` for the kernel with the largest share of the
+forward; ``cpu_baseline`` - the numpy oracle's fp32 forward on the host cores.
+
+``--impl reference`` times the reference's CPU path (the numpy restatement of
+its fp32 eager forward, oracle/) on this host instead, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd ms @268M b1 s128 (CUDA graph)"
+PUBLISHED_MS = 2.11  # reference README.md:13, RTX 5080, "TinKer fp16 + CUDA graph"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batched-steps", type=int, default=10)
+    ap.add_argument("--no-batched", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "of measured"
+    return dict(FALLBACK_PEAKS), "of fallback"
+
+
+# ------------------------------------------------------------------------------------
+# CPU side: the reference's fp32 eager forward restated in numpy (oracle/)
+# ------------------------------------------------------------------------------------
+def _blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [d.get("num_threads", 0) for d in threadpool_info() if d.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def _oracle_setup(cfg, seed=0):
+    import numpy as np
+    import oracle
+    from tinker_b200.eager_model import build_model
+    m = build_model(cfg, seed=seed)
+    w = {k: v.detach().float().numpy() for k, v in m.state_dict().items()}
+    ocfg = oracle.ModelConfig(**{f: getattr(cfg, f) for f in oracle.ModelConfig.__dataclass_fields__})
+    return oracle, w, ocfg, np
+
+
+def cpu_forward_timer(cfg, tokens, budget_s: float, max_runs: int):
+    """Median ms of the numpy fp32 forward over a bounded number of runs."""
+    oracle, w, ocfg, np = _oracle_setup(cfg)
+    tok = tokens.numpy()
+    t0 = time.perf_counter()
+    oracle.forward_logits(w, tok, ocfg)  # warm-up
+    first = time.perf_counter() - t0
+    runs = max(1, min(max_runs, int(budget_s / max(first, 1e-3))))
+    times = []
+    for _ in range(runs):
+        t = time.perf_counter()
+        oracle.forward_logits(w, tok, ocfg)
+        times.append((time.perf_counter() - t) * 1e3)
+    return statistics.median(times), runs
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the CPU reference runs once, on rank 0
+    import numpy as np
+    import oracle
+    from tinker_b200.eager_model import LLAMA_268M, make_tokens
+    cfg = LLAMA_268M
+    tokens = make_tokens(cfg, 1, 128, seed=1)
+    oracle_mod, w, ocfg, _ = _oracle_setup(cfg)
+    tok = tokens.numpy()
+    # size each step so that the whole --warmup/--steps run stays within ~3 minutes
+    t = time.perf_counter()
+    oracle.forward_logits(w, tok, ocfg)
+    full_s = time.perf_counter() - t
+    budget = 180.0 / max(1, args.steps + args.warmup)
+    layers = cfg.num_layers
+    if full_s > budget:
+        layers = max(1, int(cfg.num_layers * budget / full_s))
+    for _ in range(args.warmup):
+        oracle.forward_logits(w, tok, ocfg, num_layers=layers)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        oracle.forward_logits(w, tok, ocfg, num_layers=layers)
+        times.append((time.perf_counter() - t) * 1e3 * cfg.num_layers / layers)
+    ms = statistics.median(times)
+    sample = ("full 268M fp32 forward, batch 1 x seq 128, numpy (BLAS) restatement of the reference's eager path"
+              if layers == cfg.num_layers else
+              f"{layers} of 18 decoder layers + embedding/head per step, scaled x{cfg.num_layers / layers:.2f} to a "
+              "full 268M fp32 forward, batch 1 x seq 128, numpy restatement of the reference's eager path")
+    cores = _blas_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic: seeded N(0,0.02) weights, uniform token ids",
+        "config": {"workload": "llama268m-b1s128", "global_batch": 1, "seq_len": 128, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# GPU side
+# ------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of one GPU while the GPU is busy."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                mhz.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def _gpu_id(dev) -> str:
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return str(dev.index)
+
+
+def _dist_init(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    return rank, world, dev
+
+
+def _barrier(world):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _time_replays(graph, steps: int):
+    import torch
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record()
+    for i in range(steps):
+        graph.replay()
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+    return evs[0].elapsed_time(evs[-1]) / steps, statistics.median(per)
+
+
+def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
+    """Time each kernel kind of the forward standalone on the model's own weights (L2
+    flushed before every launch) and return (per-kind table, roofline of the largest share)."""
+    import torch
+    from tinker_b200 import _lib
+    from tinker_b200.kernels import fused_attention, fused_rmsnorm, gate_up_swiglu, linear
+    base = model._model if hasattr(model, "_model") else model
+    layers = list(base.layers)
+    M, H = tokens_per_fwd, cfg.hidden_size
+    F, D, hq, hkv = cfg.intermediate_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+    dt = next(base.parameters()).dtype
+    es = 2
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, H, device=dev, generator=g).to(dt)
+    hbuf = torch.randn(M, F, device=dev, generator=g).to(dt)
+    a = torch.randn(M, hq * D, device=dev, generator=g).to(dt)
+    qkv = torch.randn(1, M, (hq + 2 * hkv) * D, device=dev, generator=g).to(dt)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def timed(fn_list):
+        ts = []
+        for fn in fn_list:
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ts) * 1e-3  # seconds
+
+    kinds = {}
+    kinds["gate_up_swiglu"] = dict(
+        t=timed([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight) for l in layers]),
+        bytes=2 * F * H * es + M * H * es + M * F * es, flops=2 * M * H * 2 * F, per_fwd=len(layers))
+    kinds["down_proj"] = dict(
+        t=timed([lambda l=l: linear(hbuf, l.ffn.down_proj.weight) for l in layers]),
+        bytes=H * F * es + M * F * es + M * H * es, flops=2 * M * F * H, per_fwd=len(layers))
+    kinds["qkv_proj"] = dict(
+        t=timed([lambda l=l: linear(x, l.attn.q_proj.weight, l.attn.k_proj.weight, l.attn.v_proj.weight)
+                 for l in layers]),
+        bytes=(hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es,
+        flops=2 * M * H * (hq + 2 * hkv) * D, per_fwd=len(layers))
+    kinds["o_proj"] = dict(
+        t=timed([lambda l=l: linear(a, l.attn.o_proj.weight) for l in layers]),
+        bytes=H * hq * D * es + M * hq * D * es + M * H * es, flops=2 * M * hq * D * H, per_fwd=len(layers))
+    att = layers[0].attn
+    S = M
+    kinds["rope_attention"] = dict(
+        t=timed([lambda: fused_attention(qkv[..., :hq * D], qkv[..., hq * D:(hq + hkv) * D],
+                                         qkv[..., (hq + hkv) * D:], att.cos_table, att.sin_table, hq, hkv, D)
+                 for _ in layers]),
+        bytes=2 * S * D * (2 * hq + 2 * hkv), flops=2 * 2 * hq * D * S * S // 2, per_fwd=len(layers))
+    kinds["rmsnorm"] = dict(
+        t=timed([lambda l=l: fused_rmsnorm(x, l.attn_norm.weight, 1e-6) for l in layers]),
+        bytes=M * H * 2 * es + H * es, flops=4 * M * H, per_fwd=2 * len(layers) + 1)
+    table = {}
+    for k, v in kinds.items():
+        table[k] = {"us": round(v["t"] * 1e6, 2), "launches_per_fwd": v["per_fwd"],
+                    "share_us": round(v["t"] * 1e6 * v["per_fwd"], 1),
+                    "hbm_gbs": round(v["bytes"] / v["t"] / 1e9, 1),
+                    "frac_hbm": round(v["bytes"] / v["t"] / 1e9 / peaks["hbm_gbs"], 3)}
+    top = max(kinds, key=lambda k: kinds[k]["t"] * kinds[k]["per_fwd"])
+    v = kinds[top]
+    achieved = v["bytes"] / v["t"] / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(f"llama268m-b1s128/{top}")
+    roof = {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic,
+            "bytes_per_launch": v["bytes"], "note": f"peak {peak_note} (burst copy); launch timed alone, L2 flushed"}
+    return table, roof
+
+
+def run_ours(args):
+    import torch
+    import tinker_b200
+    from tinker_b200 import _lib
+    from tinker_b200.eager_model import LLAMA_268M, QWEN25_05B_SHAPED, build_model, make_tokens
+
+    rank, world, dev = _dist_init(args)
+    peaks, peak_note = _peaks()
+    cfg = LLAMA_268M
+    tokens = make_tokens(cfg, 1, 128, seed=1)
+
+    # ---- build + capture ---------------------------------------------------------------
+    cpu_model = build_model(cfg, seed=0)
+    n0 = _lib.launch_counter[0]
+    model = tinker_b200.optimize(cpu_model.to(dev), dtype=torch.float16, cuda_graph=True,
+                                 graph_input_shape=(1, 128), graph_vocab_size=cfg.vocab_size)
+    if type(model).__name__ != "_CUDAGraphWrapper":
+        raise RuntimeError("CUDA graph capture failed")
+    launches_per_fwd = (_lib.launch_counter[0] - n0) // 4  # 3 warm-up forwards + the captured one
+    model._static_input.copy_(tokens.to(dev))
+    graph = model._graph
+    sampler = ClockSampler(_gpu_id(dev))
+
+    # ---- device-resident timing ---------------------------------------------------------------
+    # warm-up; then at least ~1.5 s of replays so that the clock samples see the GPU under load
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    t_end = time.perf_counter() + 1.5
+    while time.perf_counter() < t_end:
+        for _ in range(200):
+            graph.replay()
+        torch.cuda.synchronize()
+    _barrier(world)
+    ms_mean, ms_median = _time_replays(graph, args.steps)
+    _barrier(world)
+    ms = _max_over_ranks(ms_mean, world, dev)
+
+    # ---- end to end through the public call -----------------------------------------------------
+    tok_host = tokens.pin_memory()
+    out_host = torch.empty((1, 128, cfg.vocab_size), dtype=torch.float16, pin_memory=True)
+    with torch.inference_mode():
+        for _ in range(max(3, args.warmup)):
+            out_host.copy_(model(tok_host.to(dev, non_blocking=True)), non_blocking=True)
+        _barrier(world)
+        e2e = []
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            logits = model(tok_host.to(dev, non_blocking=True))
+            out_host.copy_(logits, non_blocking=True)
+            e1.record()
+            e1.synchronize()
+            e2e.append(e0.elapsed_time(e1))
+    _barrier(world)
+    e2e_ms = _max_over_ranks(statistics.mean(e2e), world, dev)
+    clocks = sampler.stop()
+
+    # ---- per-kernel rooflines (rank 0 view; every rank runs the same work) ------------------------
+    table, roof = _kernel_rooflines(model, cfg, dev, peaks, peak_note, 128)
+    weight_bytes = sum(p.numel() * p.element_size() for p in model._model.parameters())
+    emb = model._model.embedding.weight
+    fwd_bytes = (weight_bytes - emb.numel() * emb.element_size() + 128 * cfg.hidden_size * 2
+                 + 128 * cfg.vocab_size * 2)
+    roof_fwd = {"bound": "hbm", "bytes_per_fwd": fwd_bytes, "achieved": round(fwd_bytes / (ms * 1e-3) / 1e9, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(fwd_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+                "note": f"whole forward: weights + embedding rows + logits over the replay time, {peak_note}"}
+    del model, graph, cpu_model
+    torch.cuda.empty_cache()
+
+    # ---- batched Qwen-shaped prefill, sequences split across ranks ---------------------------------
+    batched = None
+    if not args.no_batched:
+        qcfg = QWEN25_05B_SHAPED
+        per_rank = 64 // world
+        qtok = make_tokens(qcfg, 64, 512, seed=7)[rank * per_rank:(rank + 1) * per_rank]
+        qm = tinker_b200.optimize(build_model(qcfg, seed=0).to(dev), dtype=torch.bfloat16, cuda_graph=True,
+                                  graph_input_shape=(per_rank, 512), graph_vocab_size=qcfg.vocab_size,
+                                  graph_clone_output=False)
+        if type(qm).__name__ != "_CUDAGraphWrapper":
+            raise RuntimeError("CUDA graph capture failed (batched)")
+        qm._static_input.copy_(qtok.to(dev))
+        for _ in range(3):
+            qm._graph.replay()
+        _barrier(world)
+        qms, _ = _time_replays(qm._graph, args.batched_steps)
+        _barrier(world)
+        qms = _max_over_ranks(qms, world, dev)
+        flops = 2 * 64 * 512 * (qcfg.num_params() - qcfg.vocab_size * qcfg.hidden_size) \
+            + 2 * 64 * 512 * qcfg.vocab_size * qcfg.hidden_size \
+            + qcfg.num_layers * 2 * 2 * 64 * qcfg.num_heads * qcfg.head_dim * 512 * 512 // 2
+        batched = {"metric": "tokens/s Qwen2.5-0.5B-shaped bf16 prefill b64 s512 (CUDA graph)",
+                   "value": round(64 * 512 / (qms * 1e-3)), "unit": "tokens/s", "ms_per_step": round(qms, 3),
+                   "seqs_per_rank": per_rank, "scaling": "strong",
+                   "tflops": round(flops / (qms * 1e-3) / world / 1e12, 1),
+                   "frac_tensor_per_gpu": round(flops / (qms * 1e-3) / world / 1e12 / peaks["bf16_tflops_sustained"], 3),
+                   "note": f"per-GPU TFLOP/s vs the sustained bf16 peak {peak_note}; LM head via cuBLAS"}
+        del qm
+        torch.cuda.empty_cache()
+
+    # ---- CPU baseline (rank 0 at N=1) ----------------------------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_ms, runs = cpu_forward_timer(cfg, tokens, budget_s=20.0, max_runs=30)
+        cpu = {"value": round(cpu_ms, 3), "unit": "ms", "cores": _blas_threads(), "kind": "port",
+               "sample": f"{runs} full 268M fp32 forwards (b1 s128) of the numpy restatement of the reference's eager path"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": round(ms / PUBLISHED_MS, 4), "dtype": "fp16",
+            "data": "synthetic: seeded N(0,0.02) random weights, uniform token ids",
+            "config": {"workload": "llama268m-b1s128", "model": "Llama-style 268M (vocab 32000, hidden 1024, 18 layers, "
+                       "16q/4kv heads, head_dim 64, FFN 2816, untied head)", "global_batch": world, "seq_len": 128,
+                       "parallelism": f"replicas x{world} (no collective)",
+                       "l2": "no flush: each forward streams 471 MB of weights, more than the 126 MB L2"},
+            "median_step_ms": round(ms_median, 4),
+            "tokens_per_s": round(world * 128 / (ms * 1e-3)),
+            "vs_baseline_ref": f"{PUBLISHED_MS} ms, reference README.md:13 (RTX 5080)",
+            "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": 128 * 8,
+                    "d2h_bytes_per_step": 128 * cfg.vocab_size * 2},
+            "roofline": roof, "roofline_forward": roof_fwd, "kernels": table,
+            "gpu_launches": launches_per_fwd * args.steps, "gpu_launches_per_fwd": launches_per_fwd,
+            "clocks": clocks, "cpu_baseline": cpu, "batched": batched,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+/*
+ * tinker_b200.h - C ABI of the B200 (sm_100a) fused-kernel library.
+ *
+ * This library replaces everything under the reference's tinker/kernels/
+ * (eb1386/TinKer) with hand-written CUDA for sm_100a. Each entry point takes
+ * plain device pointers, element strides and sizes, a dtype code and a CUDA
+ * stream handle (cudaStream_t passed as void*; NULL = legacy default stream),
+ * enqueues its kernels on that stream and returns without synchronising, so
+ * every call may be captured in a CUDA graph. Outputs are written to
+ * caller-owned buffers; inputs are never modified.
+ *
+ * Return value: TK_OK, or an error code with a message available from
+ * tk_last_error() (per calling thread). Argument checks run on the host before
+ * any launch, so a rejected call leaves the device untouched.
+ */
+#ifndef TINKER_B200_H_
+#define TINKER_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element type codes */
+#define TK_F16 0
+#define TK_BF16 1
+#define TK_F32 2
+
+/* status codes */
+#define TK_OK 0
+#define TK_ERR_INVALID 1     /* bad shape, stride, dtype or alignment */
+#define TK_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define TK_ERR_UNSUPPORTED 3 /* not an sm_100 device, or a size the kernels do not cover */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int tk_version(void);
+
+/* Message for the last non-TK_OK return on this thread ("" if none). */
+const char* tk_last_error(void);
+
+/* TK_OK if `device` is an sm_100 (B200-class) GPU the kernels were built for. */
+int tk_check_device(int device);
+
+/* Read (and optionally clear) the sticky device-side error word of the current
+ * device. Non-zero means a kernel's bounded wait gave up (1 = timeout) and its
+ * outputs are invalid. Synchronises the device; meant for tests and debugging. */
+int tk_device_error(int* code, int clear);
+
+/*
+ * RMSNorm over the last axis: y = x * rsqrt(mean(x^2) + eps) * weight, float32
+ * statistics, one rounding to `dtype`.
+ * Replaces fused_rmsnorm / _rmsnorm_triton / _rmsnorm_kernel
+ * (tinker/kernels/fused_rmsnorm.py:70-74, :55-61, :12-52).
+ * x, y: [rows, dim] with row strides in elements; weight: [dim] of `w_dtype`.
+ * dtype, w_dtype in {TK_F16, TK_BF16, TK_F32}.
+ */
+int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int w_dtype, void* y,
+               int64_t y_row_stride, int64_t rows, int64_t dim, float eps, int dtype, void* stream);
+
+/*
+ * Residual add fused with RMSNorm: s = x + residual (rounded to dtype), written
+ * to residual_out; y = rmsnorm(s). The residual update of the reference decoder
+ * block (benchmarks/bench_e2e.py:112-115) followed by its next norm
+ * (tinker/kernels/fused_rmsnorm.py:70). All tensors contiguous [rows, dim].
+ * residual_out may alias x or residual.
+ */
+int tk_add_rmsnorm(const void* x, const void* residual, const void* weight, int w_dtype, void* y,
+                   void* residual_out, int64_t rows, int64_t dim, float eps, int dtype, void* stream);
+
+/*
+ * SwiGLU activation out = silu(gate) * up, float32 math, one rounding.
+ * Replaces fused_swiglu / _swiglu_triton / _swiglu_kernel
+ * (tinker/kernels/fused_swiglu.py:61-66, :47-54, :13-44).
+ * gate, up, out: [rows, n] with row strides in elements; dtype in {F16, BF16, F32}.
+ */
+int tk_swiglu(const void* gate, int64_t gate_row_stride, const void* up, int64_t up_row_stride, void* out,
+              int64_t out_row_stride, int64_t rows, int64_t n, int dtype, void* stream);
+
+/*
+ * Fused RoPE + GQA/MQA/MHA causal attention on tcgen05 tensor cores.
+ * Replaces fused_attention / _attention_triton / _rope_kernel / _attention_kernel
+ * (tinker/kernels/fused_attention.py:234-238, :195-231, :19-69, :74-154).
+ * q: [batch, seq, num_heads, head_dim], k, v: [batch, seq, num_kv_heads, head_dim],
+ * out: [batch, seq, num_heads, head_dim]; the *_tok_stride arguments are the
+ * element strides between consecutive tokens (so q, k and v may be column
+ * slices of one fused QKV projection). Interleaved-pair RoPE at positions
+ * start_pos + s uses cos_table/sin_table [table_rows, head_dim/2] of
+ * `table_dtype`; softmax scale 1/sqrt(head_dim); query head h reads KV head
+ * h / (num_heads / num_kv_heads). dtype in {F16, BF16}; head_dim in {64, 128}.
+ */
+int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride, const void* v,
+                      int64_t v_tok_stride, const void* cos_table, const void* sin_table, int table_dtype,
+                      int64_t table_rows, void* out, int64_t out_tok_stride, int batch, int seq, int num_heads,
+                      int num_kv_heads, int head_dim, int start_pos, int dtype, void* stream);
+
+/*
+ * y[m, n] = x[m, k] . w[n, k]^T on tcgen05 (nn.Linear without bias), fp32
+ * accumulation in TMEM. Replaces the nn.Linear projections the reference's
+ * modules run through cuBLAS (tinker/modules/attention.py:53-55,64;
+ * tinker/modules/feed_forward.py:27-30). The weight may be given as up to three
+ * row blocks w0 [n0, k], w1 [n1, k], w2 [n2, k] that are concatenated along n
+ * (n = n0 + n1 + n2; pass NULL / 0 for unused blocks), which is how the q, k and
+ * v projections run as one GEMM. Row strides in elements; dtype in {F16, BF16};
+ * k and the strides must be multiples of 8; n0, n1 multiples of 64.
+ * If residual is non-NULL, y = x . w^T + residual ([m, n], row stride y_row_stride).
+ */
+int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
+              const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
+              int64_t k, int dtype, void* stream);
+
+/*
+ * h[m, f] = silu(x . w_gate^T) * (x . w_up^T): the gate and up projections as
+ * one tcgen05 GEMM whose epilogue applies SwiGLU to the fp32 accumulators.
+ * Replaces gate_proj/up_proj + fused_swiglu in TinKerSwiGLU.forward
+ * (tinker/modules/feed_forward.py:26-30, tinker/kernels/fused_swiglu.py:61-66).
+ * x: [m, hidden] (row stride x_row_stride), w_gate, w_up: [f, hidden]
+ * contiguous, h: [m, f] contiguous. f multiple of 32, hidden multiple of 8.
+ */
+int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
+                      int64_t m, int64_t hidden, int64_t f, int dtype, void* stream);
+
+/*
+ * Whole SwiGLU FFN: out = (silu(x Wg^T) * (x Wu^T)) Wd^T (+ residual).
+ * Replaces TinKerSwiGLU.forward (tinker/modules/feed_forward.py:26-30).
+ * h_scratch is caller-provided scratch of m * f elements of dtype holding the
+ * activation between the two GEMMs. out: [m, hidden] contiguous; residual NULL
+ * or [m, hidden] contiguous (may alias out).
+ */
+int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, const void* w_down,
+                  void* h_scratch, void* out, const void* residual, int64_t m, int64_t hidden, int64_t f,
+                  int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINKER_B200_H_ */

@@ -1,0 +1,169 @@
+"""RoPE + GQA causal attention parity (tcgen05 kernel through the C ABI) vs the numpy oracle.
+
+The oracle restates the reference's eager path (fused_attention.py:176-192):
+RoPE in float32 rounded to the input dtype, K/V heads repeated per group,
+causal softmax(q k^T / sqrt(d)) v, here computed in float64. Bar (from the
+spec): norm-wise relative error <= 5e-3 per call. Cases: the reference's test
+configurations (tests/test_attention.py:84-95: tiny-gqa, plasma1.0, plasma1.1,
+MHA, MQA, seq 1, seq 128), the standalone sweep (batch x seq x head_dim x
+head layout, fp16 and bf16), ragged sequence lengths, start_pos > 0, q/k/v as
+column slices of one fused projection, and all three RoPE table dtypes.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests._util import DTYPES, NP_NAME, np32, rel_err, require_b200
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-3
+
+
+def _run(B, S, hq, hkv, d, dtype, start_pos=0, theta=1e4, table_dtype=torch.float32, seed=42, fused=False):
+    from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    if fused:
+        qkv = torch.randn(B, S, (hq + 2 * hkv) * d, device="cuda", generator=g).to(dtype)
+        q, k, v = qkv[..., :hq * d], qkv[..., hq * d:(hq + hkv) * d], qkv[..., (hq + hkv) * d:]
+    else:
+        q = torch.randn(B, S, hq * d, device="cuda", generator=g).to(dtype)
+        k = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(dtype)
+        v = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(dtype)
+    cos, sin = precompute_rope_tables(d, max(S + start_pos, 256), theta, device="cuda", dtype=table_dtype)
+    out = fused_attention(q, k, v, cos, sin, hq, hkv, d, start_pos=start_pos)
+    ref = oracle.attention(np32(q), np32(k), np32(v), np32(cos), np32(sin), hq, hkv, d, start_pos,
+                           io_dtype=NP_NAME[dtype])
+    return out, ref
+
+
+REF_CONFIGS = [
+    (256, 4, 2, 64, 32, 1), (1024, 16, 4, 64, 64, 1), (1280, 20, 4, 64, 64, 1), (512, 8, 8, 64, 64, 1),
+    (512, 8, 1, 64, 64, 1), (256, 4, 2, 64, 1, 1), (256, 4, 2, 64, 128, 1),
+]
+
+
+@pytest.mark.parametrize("hidden, hq, hkv, d, S, B", REF_CONFIGS)
+def test_reference_configs_bf16(hidden, hq, hkv, d, S, B):
+    require_b200()
+    out, ref = _run(B, S, hq, hkv, d, torch.bfloat16)
+    assert out.shape == (B, S, hq * d)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B, S", [(1, 128), (8, 512), (2, 2048)])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("hq, hkv", [(16, 4), (16, 16), (16, 1)])
+def test_sweep(dt, B, S, d, hq, hkv):
+    require_b200()
+    out, ref = _run(B, S, hq, hkv, d, DTYPES[dt], seed=B * S + d + hkv)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("S", [1, 7, 127, 129, 300])
+def test_ragged_seq(S):
+    require_b200()
+    out, ref = _run(3, S, 8, 2, 64, torch.float16, seed=S)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_start_pos_theta_and_table_dtypes(table_dtype):
+    require_b200()
+    out, ref = _run(2, 96, 14, 2, 64, torch.bfloat16, start_pos=37, theta=1e6, table_dtype=table_dtype)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_fused_qkv_views(d):
+    require_b200()
+    out, ref = _run(2, 200, 8, 2, d, torch.float16, fused=True)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+def test_single_token_returns_v():
+    """tests/test_numerical.py:88-119 of the reference: with S=1 the output is the GQA-expanded V."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
+    torch.manual_seed(7)
+    d, hq, hkv = 64, 4, 2
+    cos, sin = precompute_rope_tables(d, 16, device="cuda")
+    q = torch.randn(1, 1, hq * d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(1, 1, hkv * d, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(1, 1, hkv * d, device="cuda", dtype=torch.bfloat16)
+    out = fused_attention(q, k, v, cos, sin, hq, hkv, d)
+    exp = v.view(1, 1, hkv, d).repeat_interleave(hq // hkv, dim=2).reshape(1, 1, hq * d)
+    torch.testing.assert_close(out, exp, atol=1e-2, rtol=1e-2)
+
+
+def test_uniform_values_return_v():
+    """tests/test_numerical.py:122-156 of the reference: constant V over positions gives V."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
+    torch.manual_seed(99)
+    d, hq, hkv, S = 64, 4, 2, 16
+    cos, sin = precompute_rope_tables(d, 64, device="cuda")
+    q = torch.randn(1, S, hq * d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(1, S, hkv * d, device="cuda", dtype=torch.bfloat16)
+    v1 = torch.randn(1, 1, hkv * d, device="cuda", dtype=torch.bfloat16)
+    v = v1.expand(1, S, -1).contiguous()
+    out = fused_attention(q, k, v, cos, sin, hq, hkv, d)
+    exp = v1.view(1, 1, hkv, d).repeat_interleave(hq // hkv, dim=2).reshape(1, 1, hq * d).expand(1, S, -1)
+    torch.testing.assert_close(out, exp, atol=1e-2, rtol=1e-2)
+
+
+def test_rejects_unsupported_and_out_of_table():
+    require_b200()
+    from tinker_b200 import _lib
+    from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
+    q = torch.randn(1, 8, 4 * 32, device="cuda", dtype=torch.float16)
+    kv = torch.randn(1, 8, 2 * 32, device="cuda", dtype=torch.float16)
+    cos, sin = precompute_rope_tables(32, 16, device="cuda")
+    with pytest.raises(_lib.TinkerKernelError, match="head_dim"):
+        fused_attention(q, kv, kv, cos, sin, 4, 2, 32)
+    q = torch.randn(1, 8, 4 * 64, device="cuda", dtype=torch.float16)
+    kv = torch.randn(1, 8, 2 * 64, device="cuda", dtype=torch.float16)
+    cos, sin = precompute_rope_tables(64, 16, device="cuda")
+    with pytest.raises(_lib.TinkerKernelError, match="table"):
+        fused_attention(q, kv, kv, cos, sin, 4, 2, 64, start_pos=10)
+
+
+def test_module_matches_oracle():
+    """TinKerAttention = q|k|v GEMM + fused attention + o_proj GEMM (tests/test_attention.py:132-166)."""
+    require_b200()
+    from tinker_b200.modules import TinKerAttention
+    torch.manual_seed(42)
+    mod = TinKerAttention(1024, 16, 4, 64, max_seq_len=256).to("cuda").to(torch.bfloat16)
+    assert mod.cos_table.dtype == torch.float32
+    x = torch.randn(2, 64, 1024, device="cuda", dtype=torch.bfloat16)
+    out = mod(x)
+    xn = np32(x)
+    q = oracle.linear(xn, np32(mod.q_proj.weight), out_dtype="bfloat16")
+    k = oracle.linear(xn, np32(mod.k_proj.weight), out_dtype="bfloat16")
+    v = oracle.linear(xn, np32(mod.v_proj.weight), out_dtype="bfloat16")
+    a = oracle.attention(q, k, v, np32(mod.cos_table), np32(mod.sin_table), 16, 4, 64, io_dtype="bfloat16")
+    ref = oracle.linear(a, np32(mod.o_proj.weight), acc=np.float64)
+    assert rel_err(np32(out), ref) <= 1e-2
+
+
+def test_from_module():
+    """tests/test_attention.py:171-204 of the reference."""
+    require_b200()
+    from tinker_b200.modules import TinKerAttention
+
+    class _DummyAttention(torch.nn.Module):
+        def __init__(self, hidden, hq, hkv, d):
+            super().__init__()
+            self.head_dim = d
+            self.q_proj = torch.nn.Linear(hidden, hq * d, bias=False)
+            self.k_proj = torch.nn.Linear(hidden, hkv * d, bias=False)
+            self.v_proj = torch.nn.Linear(hidden, hkv * d, bias=False)
+            self.o_proj = torch.nn.Linear(hq * d, hidden, bias=False)
+
+    src = _DummyAttention(512, 8, 2, 64).to("cuda", torch.bfloat16)
+    mod = TinKerAttention.from_module(src).to(device="cuda", dtype=torch.bfloat16)
+    assert (mod.num_heads, mod.num_kv_heads, mod.head_dim) == (8, 2, 64)
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        torch.testing.assert_close(getattr(mod, n).weight.data, getattr(src, n).weight.data)

@@ -1,0 +1,117 @@
+"""tcgen05 GEMM parity (through the C ABI) against float64 numpy.
+
+y = x . w^T with fp32 accumulation and one rounding: the result must match the
+exactly computed product of the same half-precision inputs to within the
+output dtype's rounding (norm-wise relative error <= 1e-3 for fp16 and
+<= 4e-3 for bf16, whose unit roundoff is 2^-9), and every element to within a
+few ulps plus accumulation noise.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from tests._util import DTYPES, np32, rel_err, require_b200
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 1e-3, torch.bfloat16: 4e-3}
+
+
+def _ref(x, ws, residual=None):
+    w = np.concatenate([np32(t).astype(np.float64) for t in ws], axis=0)
+    y = np32(x).astype(np.float64).reshape(-1, w.shape[1]) @ w.T
+    if residual is not None:
+        y = y + np32(residual).astype(np.float64).reshape(y.shape)
+    return y
+
+
+SHAPES = [
+    (128, 1536, 1024),   # 268M q|k|v at batch 1 x seq 128
+    (128, 1024, 1024),   # o_proj
+    (128, 1024, 2816),   # down_proj
+    (1, 256, 64),        # single row
+    (200, 96, 40),       # ragged m, n tail, k tail (k < one k-block)
+    (4096, 896, 896),    # large m (Qwen-shaped o_proj, 8 sequences of 512)
+    (1000, 4864, 896),   # many tiles, ragged m
+    (384, 2048, 5632),   # 1B down_proj, deep k
+]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m, n, k", SHAPES)
+def test_linear(dt, m, n, k):
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(dtype)
+    y = linear(x, w)
+    assert y.shape == (m, n) and y.dtype == dtype
+    ref = _ref(x, [w])
+    assert rel_err(np32(y), ref) <= TOL[dtype]
+    np.testing.assert_allclose(np32(y), ref, rtol=4 * TOL[dtype], atol=4 * TOL[dtype] * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("hq, hkv", [(1024, 256), (896, 128), (512, 512), (512, 64)])
+@pytest.mark.parametrize("m", [128, 1030])
+def test_linear_three_weight_blocks(dt, hq, hkv, m):
+    """q|k|v projection as one GEMM over three separate weights."""
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    torch.manual_seed(hq + hkv + m)
+    k = 1024
+    x = torch.randn(m, k, device="cuda").to(dtype)
+    wq = (0.02 * torch.randn(hq, k, device="cuda")).to(dtype)
+    wk = (0.02 * torch.randn(hkv, k, device="cuda")).to(dtype)
+    wv = (0.02 * torch.randn(hkv, k, device="cuda")).to(dtype)
+    y = linear(x, wq, wk, wv)
+    assert y.shape == (m, hq + 2 * hkv)
+    assert rel_err(np32(y), _ref(x, [wq, wk, wv])) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_linear_residual_epilogue(dt):
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    torch.manual_seed(1)
+    x = torch.randn(300, 2816, device="cuda").to(dtype)
+    w = (0.02 * torch.randn(1024, 2816, device="cuda")).to(dtype)
+    r = torch.randn(300, 1024, device="cuda").to(dtype)
+    y = linear(x, w, residual=r)
+    assert rel_err(np32(y), _ref(x, [w], r)) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m, hidden, f", [(128, 1024, 2816), (4096, 2048, 5632), (77, 896, 4864), (1, 512, 1376),
+                                          (640, 256, 40)])
+def test_gate_up_swiglu(dt, m, hidden, f):
+    require_b200()
+    from tinker_b200.kernels import gate_up_swiglu
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(m + hidden + f)
+    x = torch.randn(m, hidden, device="cuda", generator=g).to(dtype)
+    wg = (0.02 * torch.randn(f, hidden, device="cuda", generator=g)).to(dtype)
+    wu = (0.02 * torch.randn(f, hidden, device="cuda", generator=g)).to(dtype)
+    h = gate_up_swiglu(x, wg, wu)
+    a = _ref(x, [wg])
+    b = _ref(x, [wu])
+    ref = a / (1 + np.exp(-a)) * b
+    assert h.shape == (m, f)
+    assert rel_err(np32(h), ref) <= TOL[dtype]
+
+
+def test_linear_rejects_bad_arguments():
+    require_b200()
+    from tinker_b200 import _lib
+    from tinker_b200.kernels import linear
+    x = torch.randn(4, 12, device="cuda", dtype=torch.float16)  # k = 12 is not a multiple of 8
+    w = torch.randn(32, 12, device="cuda", dtype=torch.float16)
+    with pytest.raises(_lib.TinkerKernelError, match="multiples of 8"):
+        linear(x, w)
+    with pytest.raises(TypeError):
+        linear(x.float(), w.float())

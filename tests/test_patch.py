@@ -1,0 +1,100 @@
+"""Host logic of the drop-in API on the CPU: module detection and replacement,
+from_module inference, state_dict compatibility, and the loud failures of the
+no-fallback design (CPU tensors, CPU models)."""
+
+import pytest
+import torch
+import torch.nn as nn
+
+import tinker_b200
+from tinker_b200.eager_model import TINY, LLAMA_268M, DecoderLM, build_model
+from tinker_b200.modules import TinKerAttention, TinKerRMSNorm, TinKerSwiGLU
+from tinker_b200.patch import _is_gqa_attention, _is_rmsnorm, _is_swiglu
+
+
+def test_detectors_follow_the_reference_rules():
+    m = build_model(TINY)
+    blk = m.layers[0]
+    assert _is_rmsnorm(blk.attn_norm) and _is_rmsnorm(m.norm)
+    assert _is_swiglu(blk.ffn) and not _is_swiglu(blk.attn)
+    assert _is_gqa_attention(blk.attn) and not _is_gqa_attention(blk.ffn)
+    assert not _is_rmsnorm(nn.LayerNorm(8))  # has a bias
+    assert not _is_rmsnorm(m.embedding)
+    hf_norm = nn.Module()
+    hf_norm.weight = nn.Parameter(torch.ones(4))
+    hf_norm.variance_epsilon = 1e-5
+    assert _is_rmsnorm(hf_norm)
+
+
+def test_patch_model_replaces_every_block_module_and_keeps_state_dict():
+    m = build_model(TINY)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    tinker_b200.patch_model(m, verbose=True)
+    kinds = [type(x).__name__ for x in m.modules()]
+    assert kinds.count("TinKerAttention") == TINY.num_layers
+    assert kinds.count("TinKerSwiGLU") == TINY.num_layers
+    assert kinds.count("TinKerRMSNorm") == 2 * TINY.num_layers + 1
+    sd2 = m.state_dict()
+    assert set(sd) == set(sd2)
+    for k in sd:
+        assert torch.equal(sd[k], sd2[k]), k
+
+
+def test_patch_flags_select_module_kinds():
+    m = build_model(TINY)
+    tinker_b200.patch_model(m, replace_attention=False, replace_ffn=False)
+    kinds = {type(x).__name__ for x in m.modules()}
+    assert "TinKerRMSNorm" in kinds and "TinKerAttention" not in kinds and "TinKerSwiGLU" not in kinds
+
+
+def test_attention_from_module_infers_heads_and_theta():
+    cfg = LLAMA_268M.with_(num_layers=1, vocab_size=16, rope_theta=1e6)
+    m = DecoderLM(cfg)
+    att = TinKerAttention.from_module(m.layers[0].attn, rope_theta=1e4, max_seq_len=512)
+    assert (att.num_heads, att.num_kv_heads, att.head_dim) == (16, 4, 64)
+    assert att.rope_theta == 1e6  # taken from the source module (attention.py:95-97)
+    assert att.cos_table.shape == (512, 32)
+
+    class NoHeadDim(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.wq = nn.Linear(256, 256, bias=False)
+            self.wk = nn.Linear(256, 128, bias=False)
+            self.wv = nn.Linear(256, 128, bias=False)
+            self.wo = nn.Linear(256, 256, bias=False)
+
+    att = TinKerAttention.from_module(NoHeadDim())
+    assert (att.num_heads, att.num_kv_heads, att.head_dim) == (4, 2, 64)
+
+
+def test_rope_tables_stay_float32_when_cast():
+    att = TinKerAttention(256, 4, 2, 64).to(torch.float16)
+    assert att.q_proj.weight.dtype == torch.float16
+    assert att.cos_table.dtype == torch.float32 and att.sin_table.dtype == torch.float32
+
+
+def test_swiglu_and_norm_from_module():
+    m = build_model(TINY)
+    f = TinKerSwiGLU.from_module(m.layers[0].ffn)
+    assert (f.hidden_size, f.intermediate_size) == (TINY.hidden_size, TINY.intermediate_size)
+    assert torch.equal(f.down_proj.weight, m.layers[0].ffn.down_proj.weight)
+    src = nn.Module()
+    src.weight = nn.Parameter(torch.randn(8))
+    src.variance_epsilon = 1e-5
+    n = TinKerRMSNorm.from_module(src)
+    assert n.eps == 1e-5 and torch.equal(n.weight, src.weight)
+    with pytest.raises(ValueError, match="SwiGLU"):
+        TinKerSwiGLU.from_module(nn.Linear(2, 2))
+
+
+def test_no_cpu_fallback():
+    m = build_model(TINY)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        tinker_b200.optimize(m)
+    tinker_b200.patch_model(m)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        m(torch.zeros(1, 4, dtype=torch.long))
+
+
+def test_param_count_of_the_268m_config():
+    assert LLAMA_268M.num_params() == 268_473_344

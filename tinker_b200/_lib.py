@@ -1,0 +1,118 @@
+"""ctypes binding of ``libtinker_b200.so``, the C-ABI kernel library.
+
+The library is loaded on first use. There is no fallback: if it is missing, or
+a call is made with tensors that are not on an sm_100 GPU, the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtinker_b200.so")
+
+TK_F16, TK_BF16, TK_F32 = 0, 1, 2
+TK_OK, TK_ERR_INVALID, TK_ERR_CUDA, TK_ERR_UNSUPPORTED = 0, 1, 2, 3
+
+_DTYPE = {torch.float16: TK_F16, torch.bfloat16: TK_BF16, torch.float32: TK_F32}
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> argtypes; every entry point returns int (status)
+SIGNATURES = {
+    "tk_version": [],
+    "tk_check_device": [_I],
+    "tk_device_error": [ctypes.POINTER(_I), _I],
+    "tk_rmsnorm": [_P, _I64, _P, _I, _P, _I64, _I64, _I64, _F, _I, _P],
+    "tk_add_rmsnorm": [_P, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _P],
+    "tk_swiglu": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P],
+    "tk_rope_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _I, _P],
+    "tk_linear": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _P],
+    "tk_gate_up_swiglu": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _P],
+    "tk_swiglu_ffn": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
+}
+
+_lock = threading.Lock()
+_lib = None
+_checked_devices: set[int] = set()
+
+
+class TinkerKernelError(RuntimeError):
+    """A call into libtinker_b200 returned an error status."""
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library (once) and declare every entry point's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is not built; run `python -m tinker_b200.build` (needs nvcc). "
+                    "tinker_b200 has no fallback path.")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.argtypes = argtypes
+                fn.restype = _I
+            L.tk_last_error.argtypes = []
+            L.tk_last_error.restype = ctypes.c_char_p
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return (lib().tk_last_error() or b"").decode(errors="replace")
+
+
+# Kernels this process has enqueued through the library (each successful
+# compute entry point adds the number of kernels it launched).
+launch_counter = [0]
+
+
+def check(rc: int, what: str, kernels: int = 0) -> None:
+    if rc != TK_OK:
+        raise TinkerKernelError(f"{what}: {last_error()} (status {rc})")
+    launch_counter[0] += kernels
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}; expected float16, bfloat16 or float32") from None
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    """All tensors on one CUDA device that is an sm_100 GPU; returns that device."""
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("tinker_b200 kernels need CUDA tensors on a B200 (sm_100a); "
+                               "there is no CPU fallback")
+        if t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {t.device} vs {dev}")
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _checked_devices:
+        check(lib().tk_check_device(idx), "tk_check_device")
+        _checked_devices.add(idx)
+    return dev
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_error(clear: bool = True) -> int:
+    """Sticky device-side error word (non-zero: a kernel's bounded wait timed out)."""
+    code = _I(0)
+    check(lib().tk_device_error(ctypes.byref(code), 1 if clear else 0), "tk_device_error")
+    return code.value

@@ -1,0 +1,429 @@
+// tcgen05 GEMM y[m, n] = x[m, k] . w[n, k]^T for the projections of the
+// decoder: the fused q|k|v projection, o_proj, the gate|up projection with the
+// SwiGLU epilogue, and down_proj (optionally adding the residual).
+//
+// Structure (one persistent CTA per SM slot, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per k-block
+//               into a STAGES-deep ring of 128-byte-swizzled shared-memory slots.
+//   warp 1      allocates TMEM; one elected lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) into one of two fp32 accumulators in TMEM and
+//               frees ring slots / publishes accumulators with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each thread owns one
+//               output row), SwiGLU or residual add in fp32, one rounding,
+//               16-byte stores. Two accumulators let the epilogue of tile i
+//               overlap the main loop of tile i+1.
+// The weight may be split into up to three row blocks (q, k and v projection
+// weights used as one GEMM without concatenating them); for the SwiGLU
+// epilogue each B tile holds BN/2 rows of the gate weight followed by the same
+// BN/2 rows of the up weight, so gate and up of one output column sit in the
+// same accumulator tile.
+#include <algorithm>
+#include <numeric>
+
+#include "tk_common.cuh"
+#include "tk_host.h"
+
+namespace tk {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of 2-byte elements
+constexpr int THREADS = 192;
+constexpr int GROUP_M = 16;  // rasterisation: GROUP_M m-tiles sweep all n-tiles together
+
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1 };
+
+struct Params {
+  int m, n, k;       // n: output columns (for SwiGLU the width of h)
+  int num_kb;        // k-blocks of BK
+  int m_tiles, n_tiles;
+  int seg1, seg2;    // first n-tile of weight block 1 and 2 (plain epilogue)
+  void* y;
+  int64_t ldy;
+  const void* residual;  // optional, [m, n] with row stride ldy
+};
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mt, int& nt) {
+  const int per_group = GROUP_M * p.n_tiles;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(p.m_tiles - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
+  static constexpr int BAR_OFF = RING;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;
+  static constexpr int TOTAL = 1024 /*align slack*/ + RING + NUM_BARS * 8 + 16;
+  static constexpr uint32_t TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128
+                                                         : (2 * BN) <= 256 ? 256 : 512;
+};
+
+template <int DT>
+__device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int col, int n, const float (&v)[32],
+                                            const void* residual) {
+  using D = Dt<DT>;
+  using T = typename D::T;
+  T* dst = reinterpret_cast<T*>(y) + static_cast<int64_t>(row) * ldy + col;
+  float o[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o[i] = v[i];
+  if (residual) {
+    const T* r = reinterpret_cast<const T*>(residual) + static_cast<int64_t>(row) * ldy + col;
+    if (col + 32 <= n) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = reinterpret_cast<const uint4*>(r)[q];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = D::unpack(*reinterpret_cast<const typename D::T2*>(&w[j]));
+          o[q * 8 + 2 * j] += f.x;
+          o[q * 8 + 2 * j + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < n) o[i] += D::to_f(r[i]);
+    }
+  }
+  if (col + 32 <= n) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        typename D::T2 h = D::pack(o[q * 8 + 2 * j], o[q * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col + i < n) dst[i] = D::from_f(o[i]);
+  }
+}
+
+template <int DT, int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+                const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tb2, const Params p) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring_a = smem;
+  uint8_t* ring_b = smem + STAGES * S::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NUM_BARS);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb0);
+      if (EPI == EPI_SWIGLU || p.seg1 < p.n_tiles) prefetch_tmap(&tb1);
+      if (EPI == EPI_STORE && p.seg2 < p.n_tiles) prefetch_tmap(&tb2);
+      const uint64_t pol_w = policy_evict_first();  // weights are streamed once per tile row
+      const uint64_t pol_a = policy_evict_last();   // activations are re-read by every n-tile
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(t, p, mt, nt);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
+          uint8_t* sa = ring_a + stage * S::A_BYTES;
+          uint8_t* sb = ring_b + stage * S::B_BYTES;
+          tma_load_2d_hint(sa, &ta, &full[stage], kb * BK, mt * BM, pol_a);
+          if constexpr (EPI == EPI_SWIGLU) {
+            tma_load_2d_hint(sb, &tb0, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+            tma_load_2d_hint(sb + (BN / 2) * 128, &tb1, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+          } else {
+            const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+            const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+            tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(Dt<DT>::umma_fmt, BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(ring_a + stage * S::A_BYTES);
+          const uint32_t b0 = smem_u32(ring_b + stage * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = make_sw128_desc(a0 + kk * 32, 0, 1024);
+            const uint64_t bd = make_sw128_desc(b0 + kk * 32, 0, 1024);
+            umma_f16_ss(d, ad, bd, idesc, (kb | kk) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++i) {
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      const int acc = i & 1;
+      const uint32_t acc_phase = (i >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      const int row = mt * BM + row_in_tile;
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------
+template <int DT, int BN, int EPI, int STAGES>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& tb2,
+           const Params& p, int ctas_per_sm, cudaStream_t st) {
+  using S = Smem<BN, STAGES>;
+  auto kern = gemm_kernel<DT, BN, EPI, STAGES>;
+  static bool configured[64] = {};
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  if (!configured[dev.device]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL),
+                            "cudaFuncSetAttribute(gemm)"))
+      return rc;
+    configured[dev.device] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = std::max(1, std::min(tiles, dev.sm_count * ctas_per_sm));
+  kern<<<grid, THREADS, S::TOTAL, st>>>(ta, tb0, tb1, tb2, p);
+  return check_launch("gemm_kernel");
+}
+
+// Largest BN (from the candidates) whose tile count still fills the GPU, else the
+// smallest: few, fat tiles when M is large; many thin tiles for weight streaming.
+static int pick_bn(int64_t m_tiles, int64_t n, int sms, const int* cands, int ncand, int64_t div_constraint) {
+  for (int i = 0; i < ncand; ++i) {
+    const int bn = cands[i];
+    if (div_constraint % bn != 0) continue;
+    const int64_t tiles = m_tiles * ((n + bn - 1) / bn);
+    if (tiles >= sms) return bn;
+  }
+  for (int i = ncand - 1; i >= 0; --i)
+    if (div_constraint % cands[i] == 0) return cands[i];
+  return 0;
+}
+
+template <int DT>
+int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const void* w1, int64_t n1, const void* w2,
+               int64_t n2, void* y, int64_t ldy, const void* residual, int64_t m, int64_t k, cudaStream_t st) {
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  const int64_t n = n0 + n1 + n2;
+  const int64_t m_tiles = (m + BM - 1) / BM;
+  // all but the last weight block must be whole tiles
+  const int64_t constraint = (n1 || n2) ? std::gcd(n0, n1 ? n1 : n0) : 256;
+  static const int cands[] = {256, 128, 64, 32};
+  const int bn = pick_bn(m_tiles, n, dev.sm_count, cands, 4, constraint);
+  if (bn == 0) return fail_invalid("linear: weight block sizes must be multiples of 32");
+  Params p{};
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.num_kb = static_cast<int>((k + BK - 1) / BK);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>((n + bn - 1) / bn);
+  p.seg1 = n1 || n2 ? static_cast<int>(n0 / bn) : p.n_tiles;
+  p.seg2 = n2 ? static_cast<int>((n0 + n1) / bn) : p.n_tiles;
+  p.y = y;
+  p.ldy = ldy;
+  p.residual = residual;
+  CUtensorMap ta, tb0, tb1, tb2;
+  if (int rc = tensor_map_2d(&ta, x, DT, m, k, lda, BM, BK)) return rc;
+  if (int rc = tensor_map_2d(&tb0, w0, DT, n0, k, k, bn, BK)) return rc;
+  tb1 = tb0;
+  tb2 = tb0;
+  if (n1)
+    if (int rc = tensor_map_2d(&tb1, w1, DT, n1, k, k, bn, BK)) return rc;
+  if (n2)
+    if (int rc = tensor_map_2d(&tb2, w2, DT, n2, k, k, bn, BK)) return rc;
+  switch (bn) {
+    case 256: return launch<DT, 256, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 1, st);
+    case 128: return launch<DT, 128, EPI_STORE, 5>(ta, tb0, tb1, tb2, p, 1, st);
+    case 64: return launch<DT, 64, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
+    default: return launch<DT, 32, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
+  }
+}
+
+template <int DT>
+int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void* h, int64_t m, int64_t hidden,
+                int64_t f, cudaStream_t st) {
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  const int64_t m_tiles = (m + BM - 1) / BM;
+  // BN counts gate + up rows; each tile produces BN/2 columns of h
+  static const int cands_half[] = {128, 64, 32, 16};
+  int half = 0;
+  for (int c : cands_half)
+    if (m_tiles * ((f + c - 1) / c) >= dev.sm_count) { half = c; break; }
+  if (!half) half = 16;
+  Params p{};
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(f);
+  p.k = static_cast<int>(hidden);
+  p.num_kb = static_cast<int>((hidden + BK - 1) / BK);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>((f + half - 1) / half);
+  p.seg1 = p.seg2 = p.n_tiles;
+  p.y = h;
+  p.ldy = f;
+  p.residual = nullptr;
+  CUtensorMap ta, tg, tu;
+  if (int rc = tensor_map_2d(&ta, x, DT, m, hidden, lda, BM, BK)) return rc;
+  if (int rc = tensor_map_2d(&tg, wg, DT, f, hidden, hidden, half, BK)) return rc;
+  if (int rc = tensor_map_2d(&tu, wu, DT, f, hidden, hidden, half, BK)) return rc;
+  switch (half) {
+    case 128: return launch<DT, 256, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 1, st);
+    case 64: return launch<DT, 128, EPI_SWIGLU, 5>(ta, tg, tu, tu, p, 1, st);
+    case 32: return launch<DT, 64, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
+    default: return launch<DT, 32, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
+  }
+}
+
+}  // namespace gemm
+}  // namespace tk
+
+using namespace tk;
+
+static int check_gemm_common(int dtype, const void* x, int64_t lda, int64_t m, int64_t k) {
+  if (!half_dtype(dtype)) return fail_invalid("GEMM dtype must be F16 or BF16");
+  if (!x) return fail_invalid("GEMM: NULL input");
+  if (m < 0 || k <= 0) return fail_invalid("GEMM: invalid m/k");
+  if (k % 8 != 0 || lda % 8 != 0) return fail_invalid("GEMM: k and the row stride must be multiples of 8");
+  if (lda < k) return fail_invalid("GEMM: row stride smaller than k");
+  if (m > 0x7fffffffLL || k > 0x7fffffffLL) return fail_invalid("GEMM: size too large");
+  return TK_OK;
+}
+
+extern "C" int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
+                         const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
+                         int64_t k, int dtype, void* stream) {
+  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
+  if (!w0 || n0 <= 0 || n1 < 0 || n2 < 0 || (n1 && !w1) || (n2 && !w2) || (n2 && !n1))
+    return fail_invalid("linear: invalid weight blocks");
+  if ((n1 || n2) && (n0 % 32 != 0 || n1 % 32 != 0)) return fail_invalid("linear: weight blocks 0 and 1 must be multiples of 32 rows");
+  const int64_t n = n0 + n1 + n2;
+  if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear: bad output or stride");
+  if (m == 0) return TK_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return gemm::run_linear<TK_F16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
+  return gemm::run_linear<TK_BF16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
+}
+
+extern "C" int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
+                                 int64_t m, int64_t hidden, int64_t f, int dtype, void* stream) {
+  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, hidden)) return rc;
+  if (!w_gate || !w_up || !h) return fail_invalid("gate_up_swiglu: NULL pointer");
+  if (f <= 0 || f % 8 != 0) return fail_invalid("gate_up_swiglu: f must be a positive multiple of 8");
+  if (m == 0) return TK_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16) return gemm::run_gate_up<TK_F16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
+  return gemm::run_gate_up<TK_BF16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
+}
+
+extern "C" int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
+                             const void* w_down, void* h_scratch, void* out, const void* residual, int64_t m,
+                             int64_t hidden, int64_t f, int dtype, void* stream) {
+  if (!w_down || !h_scratch || !out) return fail_invalid("swiglu_ffn: NULL pointer");
+  if (hidden % 8 != 0) return fail_invalid("swiglu_ffn: hidden must be a multiple of 8");
+  if (int rc = tk_gate_up_swiglu(x, x_row_stride, w_gate, w_up, h_scratch, m, hidden, f, dtype, stream)) return rc;
+  return tk_linear(h_scratch, f, w_down, hidden, nullptr, 0, nullptr, 0, out, hidden, residual, m, f, dtype, stream);
+}

@@ -1,0 +1,51 @@
+// Host-side helpers shared by the entry points: per-thread error messages,
+// argument checks, device properties, and TMA tensor-map encoding with a cache.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tinker_b200.h"
+
+namespace tk {
+
+// Record `msg` as this thread's last error and return `code`.
+int set_error(int code, const std::string& msg);
+inline int fail_invalid(const std::string& msg) { return set_error(TK_ERR_INVALID, msg); }
+
+// Check a CUDA runtime status; on failure records it and returns TK_ERR_CUDA.
+int check_cuda(cudaError_t e, const char* what);
+
+// Launch-error check after a <<<>>> launch.
+inline int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int major = 0;
+  int minor = 0;
+  size_t smem_optin = 0;
+};
+// Properties of the current device (cached per device).
+int current_device_info(DeviceInfo* out);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline int elem_size(int dt) { return dt == TK_F32 ? 4 : 2; }
+inline bool valid_dtype(int dt) { return dt == TK_F16 || dt == TK_BF16 || dt == TK_F32; }
+inline bool half_dtype(int dt) { return dt == TK_F16 || dt == TK_BF16; }
+
+// 2-D tensor map over a row-major [rows, cols] matrix of 2-byte elements
+// (row stride in elements), box [box_rows, box_cols], 128-byte swizzle.
+// Cached by all of its arguments, so repeated calls with the same buffer are cheap.
+int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                  uint64_t row_stride, uint32_t box_rows, uint32_t box_cols);
+
+// 3-D tensor map over [d2, d1, d0] (d0 contiguous) with strides s1, s2 in
+// elements, box [b2, b1, b0], 128-byte swizzle.
+int tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d0, uint64_t d1, uint64_t d2,
+                  uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
+
+}  // namespace tk

@@ -1,0 +1,9 @@
+"""sm_100a kernels (the replacement of the reference's tinker/kernels package)."""
+
+from tinker_b200.kernels.fused_rmsnorm import fused_rmsnorm, fused_add_rmsnorm
+from tinker_b200.kernels.fused_swiglu import fused_swiglu
+from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
+from tinker_b200.kernels.gemm import linear, gate_up_swiglu, swiglu_ffn
+
+__all__ = ["fused_rmsnorm", "fused_swiglu", "fused_attention", "precompute_rope_tables",
+           "fused_add_rmsnorm", "linear", "gate_up_swiglu", "swiglu_ffn"]

@@ -1,0 +1,112 @@
+"""tcgen05 GEMMs for the projections (tinker_b200/csrc/gemm.cu).
+
+The reference runs every projection through ``nn.Linear`` / cuBLAS
+(eb1386/TinKer tinker/modules/attention.py:53-55,64 and
+tinker/modules/feed_forward.py:27-30). Here they are hand-written sm_100a GEMMs:
+
+* ``linear(x, w0, w1=None, w2=None, residual=None)`` - ``x @ cat(w0, w1, w2).T``
+  without materialising the concatenation (the fused q|k|v projection), with an
+  optional residual add in the epilogue.
+* ``gate_up_swiglu(x, w_gate, w_up)`` - ``silu(x @ w_gate.T) * (x @ w_up.T)`` as one
+  GEMM with the SwiGLU applied to the fp32 accumulators.
+* ``swiglu_ffn(x, w_gate, w_up, w_down, residual=None)`` - the whole FFN.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from tinker_b200 import _lib
+from tinker_b200.kernels._common import call_ctx, row_stride, rows_view
+
+
+def _check_w(w: torch.Tensor, k: int, dtype) -> torch.Tensor:
+    if w.dim() != 2 or w.shape[1] != k:
+        raise ValueError(f"weight must be [n, {k}], got {tuple(w.shape)}")
+    if w.dtype != dtype:
+        raise TypeError(f"weight dtype {w.dtype} does not match input dtype {dtype}")
+    return w if w.is_contiguous() else w.contiguous()
+
+
+def _check_x(x: torch.Tensor) -> torch.Tensor:
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("tinker_b200 GEMMs take float16 or bfloat16 inputs")
+    x2 = rows_view(x)
+    if row_stride(x2) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    return x2
+
+
+def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2: torch.Tensor | None = None,
+           residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ cat([w0, w1, w2]).T (+ residual)``; x [..., k], w* [n*, k]."""
+    ws = [w for w in (w0, w1, w2) if w is not None]
+    dev = _lib.require_cuda(x, *ws)
+    x2 = _check_x(x)
+    k = x2.shape[1]
+    ws = [_check_w(w, k, x.dtype) for w in ws]
+    n = sum(w.shape[0] for w in ws)
+    m = x2.shape[0]
+    lead = x.shape[:-1]
+    if out is None:
+        out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    elif out.shape != (m, n) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [m, n] tensor")
+    r = None
+    if residual is not None:
+        r = residual.reshape(m, n)
+        if not r.is_contiguous() or r.dtype != x.dtype:
+            r = r.contiguous().to(x.dtype)
+    ptrs = [w.data_ptr() for w in ws] + [None] * (3 - len(ws))
+    rows = [w.shape[0] for w in ws] + [0] * (3 - len(ws))
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_linear(x2.data_ptr(), row_stride(x2), ptrs[0], rows[0], ptrs[1], rows[1], ptrs[2],
+                                        rows[2], out.data_ptr(), n, None if r is None else r.data_ptr(), m, k,
+                                        _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear", 1)
+    return out.reshape(*lead, n)
+
+
+def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """``silu(x @ w_gate.T) * (x @ w_up.T)`` as one GEMM with a SwiGLU epilogue."""
+    dev = _lib.require_cuda(x, w_gate, w_up)
+    x2 = _check_x(x)
+    k = x2.shape[1]
+    wg, wu = _check_w(w_gate, k, x.dtype), _check_w(w_up, k, x.dtype)
+    if wg.shape != wu.shape:
+        raise ValueError("gate and up weights must have the same shape")
+    f = wg.shape[0]
+    h = torch.empty(x2.shape[0], f, dtype=x.dtype, device=x.device)
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_gate_up_swiglu(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
+                                                h.data_ptr(), x2.shape[0], k, f, _lib.dtype_code(x.dtype),
+                                                _lib.stream_ptr(dev)), "tk_gate_up_swiglu", 1)
+    return h.reshape(*x.shape[:-1], f)
+
+
+def swiglu_ffn(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
+               residual: torch.Tensor | None = None) -> torch.Tensor:
+    """``down(silu(gate(x)) * up(x)) (+ residual)``: gate|up GEMM with SwiGLU epilogue, then down GEMM.
+
+    The [m, f] activation between the two GEMMs is scratch memory allocated here
+    from PyTorch's caching allocator.
+    """
+    dev = _lib.require_cuda(x, w_gate, w_up, w_down)
+    x2 = _check_x(x)
+    k = x2.shape[1]
+    wg, wu = _check_w(w_gate, k, x.dtype), _check_w(w_up, k, x.dtype)
+    f = wg.shape[0]
+    wd = _check_w(w_down, f, x.dtype)
+    if wd.shape[0] != k:
+        raise ValueError("down projection must map back to the hidden size")
+    m = x2.shape[0]
+    h = torch.empty(m, f, dtype=x.dtype, device=x.device)
+    out = torch.empty(m, k, dtype=x.dtype, device=x.device)
+    r = None
+    if residual is not None:
+        r = residual.reshape(m, k).contiguous()
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_swiglu_ffn(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
+                                            wd.data_ptr(), h.data_ptr(), out.data_ptr(),
+                                            None if r is None else r.data_ptr(), m, k, f,
+                                            _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_swiglu_ffn", 2)
+    return out.reshape(*x.shape[:-1], k)

@@ -1,0 +1,186 @@
+"""model optimizer - the main api (drop-in for eb1386/TinKer tinker/optimize.py:27-242).
+
+``optimize`` applies, in the reference's order:
+  1. module patching: RMSNorm / SwiGLU FFN / GQA attention -> ``TinKer*`` modules
+     running the sm_100a kernels (the reference gates this on Triton being
+     importable; here it needs the built kernel library and a B200)
+  2. half precision (``dtype``)
+  3. int8 dynamic quantization: not part of the B200 path (the reference's is a
+     CPU-only ``quantize_dynamic``); reported and skipped
+  4. ``compile``: accepted and not used - the patched forward already runs
+     hand-written kernels, and the CUDA graph removes the launch overhead
+  5. CUDA backend flags (TF32, cuDNN benchmark, flash SDPA) as in the reference
+  6. optional CUDA graph capture of the whole forward (static shapes)
+"""
+
+import time
+
+import torch
+import torch.nn as nn
+
+from tinker_b200 import _lib
+from tinker_b200.patch import patch_model
+
+
+def optimize(
+    model: nn.Module,
+    dtype: torch.dtype | None = None,
+    compile: bool | None = None,
+    compile_mode: str = "reduce-overhead",
+    quantize: bool = False,
+    replace_attention: bool = True,
+    replace_ffn: bool = True,
+    replace_norm: bool = True,
+    rope_theta: float = 10000.0,
+    max_seq_len: int = 2048,
+    cuda_graph: bool = False,
+    graph_input_shape: tuple | None = None,
+    graph_vocab_size: int = 32000,
+    verbose: bool = False,
+    graph_clone_output: bool = True,
+) -> nn.Module:
+    """optimize a model for inference on a B200.
+
+    Same arguments as the reference. ``graph_clone_output`` (extra, default True
+    as in the reference) controls whether the CUDA-graph wrapper returns a clone
+    of its static output or the static output itself.
+    """
+    model.eval()
+    params = list(model.parameters())
+    if not params or not params[0].is_cuda:
+        raise RuntimeError("tinker_b200.optimize needs the model on a CUDA device (B200, sm_100a); "
+                           "move it with model.to('cuda') first")
+    _lib.require_cuda(params[0])
+
+    if verbose:
+        print("[tinker] patching modules (sm_100a fused kernels)...")
+    model = patch_model(
+        model,
+        replace_attention=replace_attention,
+        replace_ffn=replace_ffn,
+        replace_norm=replace_norm,
+        rope_theta=rope_theta,
+        max_seq_len=max_seq_len,
+        verbose=verbose,
+    )
+
+    if dtype is not None:
+        if verbose:
+            print(f"  [tinker] casting to {dtype}")
+        model = model.to(dtype=dtype)
+
+    if quantize and verbose:
+        print("  [tinker] int8 quantization skipped: not part of the B200 kernel path")
+
+    if compile and verbose:
+        print(f"  [tinker] torch.compile (mode={compile_mode}) not used: the forward runs sm_100a kernels")
+
+    torch.backends.cudnn.benchmark = True
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    torch.set_float32_matmul_precision("high")
+    torch.backends.cuda.enable_flash_sdp(True)
+    torch.backends.cuda.enable_mem_efficient_sdp(True)
+    if verbose:
+        print("  [tinker] cuda: tf32 + cudnn benchmark + flash sdpa")
+
+    for p in model.parameters():
+        p.requires_grad_(False)
+    if verbose:
+        print("  [tinker] disabled gradients")
+
+    if cuda_graph:
+        if graph_input_shape is not None:
+            model = _capture_cuda_graph(model, graph_input_shape, graph_vocab_size, verbose=verbose,
+                                        clone_output=graph_clone_output)
+        elif verbose:
+            print("  [tinker] skipping cuda graph (no input shape)")
+
+    if verbose:
+        print(f"\n  [tinker] ready (sm_100a kernels + {torch.cuda.get_device_name(params[0].device)})")
+    return model
+
+
+class _CUDAGraphWrapper(nn.Module):
+    """wraps model with cuda graph replay (optimize.py:134-150)"""
+
+    def __init__(self, model, static_input, static_output, graph, clone_output=True):
+        super().__init__()
+        self._model = model
+        self._static_input = static_input
+        self._static_output = static_output
+        self._graph = graph
+        self._input_shape = static_input.shape
+        self._clone_output = clone_output
+
+    def forward(self, x):
+        if x.shape == self._input_shape:
+            self._static_input.copy_(x, non_blocking=True)
+            self._graph.replay()
+            return self._static_output.clone() if self._clone_output else self._static_output
+        return self._model(x)
+
+
+def _capture_cuda_graph(model, input_shape, vocab_size, verbose=False, clone_output=True):
+    """capture cuda graph: 3 warm-up forwards, then one captured forward (optimize.py:153-173)"""
+    try:
+        device = next(model.parameters()).device
+        static_input = torch.randint(0, vocab_size, input_shape, device=device)
+        with torch.inference_mode():
+            for _ in range(3):
+                _ = model(static_input)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                static_output = model(static_input)
+        if verbose:
+            print(f"  [tinker] cuda graph captured (shape={input_shape})")
+        return _CUDAGraphWrapper(model, static_input, static_output, graph, clone_output)
+    except Exception as e:
+        if verbose:
+            print(f"  [tinker] cuda graph failed: {e}")
+        return model
+
+
+@torch.inference_mode()
+def benchmark_model(
+    model: nn.Module,
+    input_shape: tuple = (1, 128),
+    vocab_size: int = 32000,
+    warmup: int = 10,
+    runs: int = 100,
+    device: str | None = None,
+) -> dict:
+    """benchmark forward pass latency (optimize.py:190-242: median of `runs`, synchronised wall clock)"""
+    if device is None:
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    tokens = torch.randint(0, vocab_size, input_shape, device=device)
+    for _ in range(warmup):
+        _ = model(tokens)
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+    times = []
+    for _ in range(runs):
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _ = model(tokens)
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        times.append((time.perf_counter() - t0) * 1000)
+    times.sort()
+    median = times[len(times) // 2]
+    mean = sum(times) / len(times)
+    tps = input_shape[0] * input_shape[1] / (median / 1000)
+    result = {
+        "median_ms": round(median, 3),
+        "mean_ms": round(mean, 3),
+        "min_ms": round(times[0], 3),
+        "tokens_per_sec": round(tps),
+        "device": device,
+    }
+    if torch.cuda.is_available():
+        result["peak_memory_mb"] = round(torch.cuda.max_memory_allocated() / (1024 ** 2), 1)
+        result["gpu"] = torch.cuda.get_device_name(0)
+    return result
