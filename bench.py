@@ -49,6 +49,9 @@ def _args():
     ap.add_argument("--batched-steps", type=int, default=10)
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["forward", "gate_up_swiglu", "down_proj", "qkv_proj", "o_proj",
+                                       "rope_attention", "rmsnorm"],
+                    help="profiling helper: time only the graph replay or one kernel kind (268M shapes)")
     return ap.parse_args()
 
 
@@ -244,11 +247,10 @@ def _time_replays(graph, steps: int):
     return evs[0].elapsed_time(evs[-1]) / steps, statistics.median(per)
 
 
-def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
-    """Time each kernel kind of the forward standalone on the model's own weights (L2
-    flushed before every launch) and return (per-kind table, roofline of the largest share)."""
+def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
+    """For each kernel kind of the forward: (one closure per layer launching it on that
+    layer's weights, algorithmic bytes per launch, flops per launch, launches per forward)."""
     import torch
-    from tinker_b200 import _lib
     from tinker_b200.kernels import fused_attention, fused_rmsnorm, gate_up_swiglu, linear
     base = model._model if hasattr(model, "_model") else model
     layers = list(base.layers)
@@ -261,12 +263,40 @@ def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
     hbuf = torch.randn(M, F, device=dev, generator=g).to(dt)
     a = torch.randn(M, hq * D, device=dev, generator=g).to(dt)
     qkv = torch.randn(1, M, (hq + 2 * hkv) * D, device=dev, generator=g).to(dt)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    att = layers[0].attn
+    S = M
+    return {
+        "gate_up_swiglu": ([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight)
+                            for l in layers], 2 * F * H * es + M * H * es + M * F * es, 2 * M * H * 2 * F, len(layers)),
+        "down_proj": ([lambda l=l: linear(hbuf, l.ffn.down_proj.weight) for l in layers],
+                      H * F * es + M * F * es + M * H * es, 2 * M * F * H, len(layers)),
+        "qkv_proj": ([lambda l=l: linear(x, l.attn.q_proj.weight, l.attn.k_proj.weight, l.attn.v_proj.weight)
+                      for l in layers], (hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es,
+                     2 * M * H * (hq + 2 * hkv) * D, len(layers)),
+        "o_proj": ([lambda l=l: linear(a, l.attn.o_proj.weight) for l in layers],
+                   H * hq * D * es + M * hq * D * es + M * H * es, 2 * M * hq * D * H, len(layers)),
+        "rope_attention": ([lambda: fused_attention(qkv[..., :hq * D], qkv[..., hq * D:(hq + hkv) * D],
+                                                    qkv[..., (hq + hkv) * D:], att.cos_table, att.sin_table,
+                                                    hq, hkv, D) for _ in layers],
+                           2 * S * D * (2 * hq + 2 * hkv), 2 * 2 * hq * D * S * S // 2, len(layers)),
+        "rmsnorm": ([lambda l=l: fused_rmsnorm(x, l.attn_norm.weight, 1e-6) for l in layers],
+                    M * H * 2 * es + H * es, 4 * M * H, 2 * len(layers) + 1),
+    }
+
+
+def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
+    """Time each kernel kind standalone on the model's own weights, L2 flushed (by reading a
+    buffer larger than L2) before every launch; return (per-kind table, roofline of the
+    kind with the largest share of the forward)."""
+    import torch
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
+    flush.zero_()
+    sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def timed(fn_list):
         ts = []
         for fn in fn_list:
-            flush.zero_()
+            torch.sum(flush, out=sink)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             fn()
@@ -276,30 +306,9 @@ def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
         return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ts) * 1e-3  # seconds
 
     kinds = {}
-    kinds["gate_up_swiglu"] = dict(
-        t=timed([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight) for l in layers]),
-        bytes=2 * F * H * es + M * H * es + M * F * es, flops=2 * M * H * 2 * F, per_fwd=len(layers))
-    kinds["down_proj"] = dict(
-        t=timed([lambda l=l: linear(hbuf, l.ffn.down_proj.weight) for l in layers]),
-        bytes=H * F * es + M * F * es + M * H * es, flops=2 * M * F * H, per_fwd=len(layers))
-    kinds["qkv_proj"] = dict(
-        t=timed([lambda l=l: linear(x, l.attn.q_proj.weight, l.attn.k_proj.weight, l.attn.v_proj.weight)
-                 for l in layers]),
-        bytes=(hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es,
-        flops=2 * M * H * (hq + 2 * hkv) * D, per_fwd=len(layers))
-    kinds["o_proj"] = dict(
-        t=timed([lambda l=l: linear(a, l.attn.o_proj.weight) for l in layers]),
-        bytes=H * hq * D * es + M * hq * D * es + M * H * es, flops=2 * M * hq * D * H, per_fwd=len(layers))
-    att = layers[0].attn
-    S = M
-    kinds["rope_attention"] = dict(
-        t=timed([lambda: fused_attention(qkv[..., :hq * D], qkv[..., hq * D:(hq + hkv) * D],
-                                         qkv[..., (hq + hkv) * D:], att.cos_table, att.sin_table, hq, hkv, D)
-                 for _ in layers]),
-        bytes=2 * S * D * (2 * hq + 2 * hkv), flops=2 * 2 * hq * D * S * S // 2, per_fwd=len(layers))
-    kinds["rmsnorm"] = dict(
-        t=timed([lambda l=l: fused_rmsnorm(x, l.attn_norm.weight, 1e-6) for l in layers]),
-        bytes=M * H * 2 * es + H * es, flops=4 * M * H, per_fwd=2 * len(layers) + 1)
+    for name, (fns, nbytes, flops, per_fwd) in _kernel_cases(model, cfg, dev, tokens_per_fwd).items():
+        timed(fns[:2])  # first-launch set-up (kernel attributes, tensor maps)
+        kinds[name] = dict(t=timed(fns), bytes=nbytes, flops=flops, per_fwd=per_fwd)
     table = {}
     for k, v in kinds.items():
         table[k] = {"us": round(v["t"] * 1e6, 2), "launches_per_fwd": v["per_fwd"],
@@ -318,6 +327,39 @@ def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
             "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic,
             "bytes_per_launch": v["bytes"], "note": f"peak {peak_note} (burst copy); launch timed alone, L2 flushed"}
     return table, roof
+
+
+def run_only(args):
+    """Profiling helper: run just one forward replay loop, or one kernel kind, on the 268M
+    shapes (``--only forward`` / ``--only gate_up_swiglu`` ...) and print its mean time."""
+    import torch
+    import tinker_b200
+    from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = LLAMA_268M
+    tokens = make_tokens(cfg, 1, 128, seed=1)
+    graph = args.only == "forward"
+    model = tinker_b200.optimize(build_model(cfg, seed=0).to(dev), dtype=torch.float16, cuda_graph=graph,
+                                 graph_input_shape=(1, 128), graph_vocab_size=cfg.vocab_size)
+    if graph:
+        model._static_input.copy_(tokens.to(dev))
+        for _ in range(args.warmup):
+            model._graph.replay()
+        ms, _ = _time_replays(model._graph, args.steps)
+    else:
+        fns = _kernel_cases(model, cfg, dev, 128)[args.only][0]
+        for i in range(args.warmup):
+            fns[i % len(fns)]()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fns[i % len(fns)]()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"only": args.only, "steps": args.steps, "ms_mean": round(ms, 5)}), flush=True)
 
 
 def run_ours(args):
@@ -457,6 +499,8 @@ def main():
     args = _args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args)
 

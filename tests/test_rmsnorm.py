@@ -25,7 +25,9 @@ def _check(y, x, w, eps, dtype):
     exact = oracle.rmsnorm(np32(x), np32(w), eps)
     yy = np32(y)
     np.testing.assert_allclose(yy, ref, rtol=ulp(dtype), atol=1e-6 if dtype == torch.float32 else ulp(dtype) * 1e-2)
-    assert rel_err(yy, exact) <= 1e-3
+    # <= 1e-3 relative to the float32 result; a bf16 output cannot do better than its own
+    # rounding (~1.6e-3 for these values), so there the bar is correct rounding (+1%)
+    assert rel_err(yy, exact) <= max(1e-3, 1.01 * rel_err(ref, exact))
 
 
 @pytest.mark.parametrize("dim, seq, batch", REF_CONFIGS)

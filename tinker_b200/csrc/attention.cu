@@ -338,7 +338,6 @@ extern "C" int tk_rope_attention(const void* q, int64_t q_tok_stride, const void
   using namespace tk;
   if (!half_dtype(dtype)) return fail_invalid("rope_attention: dtype must be F16 or BF16");
   if (!valid_dtype(table_dtype)) return fail_invalid("rope_attention: table dtype must be F16, BF16 or F32");
-  if (!q || !k || !v || !cos_table || !sin_table || !out) return fail_invalid("rope_attention: NULL pointer");
   if (head_dim != 64 && head_dim != 128) return set_error(TK_ERR_UNSUPPORTED, "rope_attention: head_dim must be 64 or 128");
   if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || start_pos < 0)
     return fail_invalid("rope_attention: invalid sizes");
@@ -348,12 +347,13 @@ extern "C" int tk_rope_attention(const void* q, int64_t q_tok_stride, const void
     return fail_invalid("rope_attention: token stride smaller than heads * head_dim");
   if (q_tok_stride % 8 || k_tok_stride % 8 || v_tok_stride % 8 || out_tok_stride % 8)
     return fail_invalid("rope_attention: token strides must be multiples of 8 elements");
-  if (!aligned16(out) || !aligned16(cos_table) || !aligned16(sin_table))
-    return fail_invalid("rope_attention: out and the RoPE tables must be 16-byte aligned");
   if (int64_t(start_pos) + seq > table_rows)
     return fail_invalid("rope_attention: start_pos + seq exceeds the RoPE table length");
   if (num_heads > 65535 || batch > 65535) return fail_invalid("rope_attention: too many heads or batches");
-  if (batch == 0 || seq == 0) return TK_OK;
+  if (batch == 0 || seq == 0) return TK_OK;  // empty tensors may carry NULL data pointers
+  if (!q || !k || !v || !cos_table || !sin_table || !out) return fail_invalid("rope_attention: NULL pointer");
+  if (!aligned16(out) || !aligned16(cos_table) || !aligned16(sin_table))
+    return fail_invalid("rope_attention: out and the RoPE tables must be 16-byte aligned");
   attn::Params p{};
   p.batch = batch;
   p.seq = seq;

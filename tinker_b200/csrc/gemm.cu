@@ -112,6 +112,30 @@ __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int c
   }
 }
 
+// First 16 values of v to columns [col, col + 16) of row `row` (columns >= n dropped).
+template <int DT>
+__device__ __forceinline__ void store_row16(void* y, int64_t ldy, int row, int col, int n, const float* v) {
+  using D = Dt<DT>;
+  using T = typename D::T;
+  T* dst = reinterpret_cast<T*>(y) + static_cast<int64_t>(row) * ldy + col;
+  if (col + 16 <= n) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        typename D::T2 h = D::pack(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (col + i < n) dst[i] = D::from_f(v[i]);
+  }
+}
+
 template <int DT, int BN, int EPI, int STAGES>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
@@ -230,7 +254,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       const int row = mt * BM + row_in_tile;
-      if constexpr (EPI == EPI_SWIGLU) {
+      if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
+        // 16 gate columns followed by 16 up columns
+        float g[32], u[16];
+        tmem_ld16(taddr, g);
+        tmem_ld16(taddr + BN / 2, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+        if (row < p.m) store_row16<DT>(p.y, p.ldy, row, nt * (BN / 2), p.n, g);
+      } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float g[32], u[32];
@@ -384,8 +417,8 @@ using namespace tk;
 
 static int check_gemm_common(int dtype, const void* x, int64_t lda, int64_t m, int64_t k) {
   if (!half_dtype(dtype)) return fail_invalid("GEMM dtype must be F16 or BF16");
-  if (!x) return fail_invalid("GEMM: NULL input");
   if (m < 0 || k <= 0) return fail_invalid("GEMM: invalid m/k");
+  if (!x && m > 0) return fail_invalid("GEMM: NULL input");
   if (k % 8 != 0 || lda % 8 != 0) return fail_invalid("GEMM: k and the row stride must be multiples of 8");
   if (lda < k) return fail_invalid("GEMM: row stride smaller than k");
   if (m > 0x7fffffffLL || k > 0x7fffffffLL) return fail_invalid("GEMM: size too large");
@@ -396,8 +429,9 @@ extern "C" int tk_linear(const void* x, int64_t x_row_stride, const void* w0, in
                          const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
                          int64_t k, int dtype, void* stream) {
   if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
-  if (!w0 || n0 <= 0 || n1 < 0 || n2 < 0 || (n1 && !w1) || (n2 && !w2) || (n2 && !n1))
-    return fail_invalid("linear: invalid weight blocks");
+  if (n0 <= 0 || n1 < 0 || n2 < 0 || (n2 && !n1)) return fail_invalid("linear: invalid weight blocks");
+  if (m == 0) return TK_OK;
+  if (!w0 || (n1 && !w1) || (n2 && !w2)) return fail_invalid("linear: NULL weight");
   if ((n1 || n2) && (n0 % 32 != 0 || n1 % 32 != 0)) return fail_invalid("linear: weight blocks 0 and 1 must be multiples of 32 rows");
   const int64_t n = n0 + n1 + n2;
   if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear: bad output or stride");
@@ -411,9 +445,9 @@ extern "C" int tk_linear(const void* x, int64_t x_row_stride, const void* w0, in
 extern "C" int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
                                  int64_t m, int64_t hidden, int64_t f, int dtype, void* stream) {
   if (int rc = check_gemm_common(dtype, x, x_row_stride, m, hidden)) return rc;
-  if (!w_gate || !w_up || !h) return fail_invalid("gate_up_swiglu: NULL pointer");
   if (f <= 0 || f % 8 != 0) return fail_invalid("gate_up_swiglu: f must be a positive multiple of 8");
   if (m == 0) return TK_OK;
+  if (!w_gate || !w_up || !h) return fail_invalid("gate_up_swiglu: NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TK_F16) return gemm::run_gate_up<TK_F16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
   return gemm::run_gate_up<TK_BF16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
@@ -422,8 +456,9 @@ extern "C" int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void
 extern "C" int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
                              const void* w_down, void* h_scratch, void* out, const void* residual, int64_t m,
                              int64_t hidden, int64_t f, int dtype, void* stream) {
-  if (!w_down || !h_scratch || !out) return fail_invalid("swiglu_ffn: NULL pointer");
   if (hidden % 8 != 0) return fail_invalid("swiglu_ffn: hidden must be a multiple of 8");
+  if (m == 0) return TK_OK;
+  if (!w_down || !h_scratch || !out) return fail_invalid("swiglu_ffn: NULL pointer");
   if (int rc = tk_gate_up_swiglu(x, x_row_stride, w_gate, w_up, h_scratch, m, hidden, f, dtype, stream)) return rc;
   return tk_linear(h_scratch, f, w_down, hidden, nullptr, 0, nullptr, 0, out, hidden, residual, m, f, dtype, stream);
 }

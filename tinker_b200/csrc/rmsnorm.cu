@@ -97,12 +97,12 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const void* __restrict
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if constexpr (WARPS > 1) {
-    // one row per block when TPR > 32 (blockDim.y == 1)
-    if ((t & 31) == 0) red[t >> 5] = ss;
+    // a row spans WARPS warps; blockDim.y rows share the block, each with its own slots
+    if ((t & 31) == 0) red[threadIdx.y * WARPS + (t >> 5)] = ss;
     __syncthreads();
     ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < WARPS; ++i) ss += red[i];
+    for (int i = 0; i < WARPS; ++i) ss += red[threadIdx.y * WARPS + i];
   }
   const float rrms = rsqrtf(ss / static_cast<float>(dim) + eps);
   if (!active) return;
@@ -189,10 +189,10 @@ int rmsnorm_dispatch(const void* x, int64_t xs, const void* res, const void* w, 
                      void* res_out, int64_t rows, int64_t dim, float eps, int dtype, void* stream) {
   if (!valid_dtype(dtype) || !valid_dtype(wdt)) return fail_invalid("rmsnorm: dtype must be F16, BF16 or F32");
   if (rows < 0 || dim <= 0 || dim > (1 << 24)) return fail_invalid("rmsnorm: invalid rows/dim");
-  if (!x || !w || !y || (ADD && (!res || !res_out))) return fail_invalid("rmsnorm: NULL pointer");
   if (xs < dim || ys < dim) return fail_invalid("rmsnorm: row stride smaller than dim");
   if (!(eps >= 0.f)) return fail_invalid("rmsnorm: eps must be >= 0");
-  if (rows == 0) return TK_OK;
+  if (rows == 0) return TK_OK;  // empty tensors may carry NULL data pointers
+  if (!x || !w || !y || (ADD && (!res || !res_out))) return fail_invalid("rmsnorm: NULL pointer");
   if (rows > 0x7fffffffLL) return fail_invalid("rmsnorm: too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
@@ -280,11 +280,11 @@ extern "C" int tk_swiglu(const void* gate, int64_t gate_row_stride, const void* 
                          int64_t out_row_stride, int64_t rows, int64_t n, int dtype, void* stream) {
   using namespace tk;
   if (!valid_dtype(dtype)) return fail_invalid("swiglu: dtype must be F16, BF16 or F32");
-  if (!gate || !up || !out) return fail_invalid("swiglu: NULL pointer");
   if (rows < 0 || n < 0) return fail_invalid("swiglu: negative size");
   if (gate_row_stride < n || up_row_stride < n || out_row_stride < n)
     return fail_invalid("swiglu: row stride smaller than n");
-  if (rows == 0 || n == 0) return TK_OK;
+  if (rows == 0 || n == 0) return TK_OK;  // empty tensors may carry NULL data pointers
+  if (!gate || !up || !out) return fail_invalid("swiglu: NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case TK_F16: return launch_swiglu<TK_F16>(gate, gate_row_stride, up, up_row_stride, out, out_row_stride, rows, n, st);
