@@ -5,9 +5,8 @@
  * (eb1386/TinKer) with hand-written CUDA for sm_100a. Each entry point takes
  * plain device pointers, element strides and sizes, a dtype code and a CUDA
  * stream handle (cudaStream_t passed as void*; NULL = legacy default stream),
- * enqueues its kernels on that stream and returns without synchronising, so
- * every call may be captured in a CUDA graph. Outputs are written to
- * caller-owned buffers; inputs are never modified.
+ * enqueues its kernels on that stream and returns without synchronising.
+ * Outputs are written to caller-owned buffers; inputs are never modified.
  *
  * Return value: TK_OK, or an error code with a message available from
  * tk_last_error() (per calling thread). Argument checks run on the host before
@@ -102,7 +101,7 @@ int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k, int64_
  * row blocks w0 [n0, k], w1 [n1, k], w2 [n2, k] that are concatenated along n
  * (n = n0 + n1 + n2; pass NULL / 0 for unused blocks), which is how the q, k and
  * v projections run as one GEMM. Row strides in elements; dtype in {F16, BF16};
- * k and the strides must be multiples of 8; n0, n1 multiples of 64.
+ * k and the strides must be multiples of 8; n0, n1 multiples of 32.
  * If residual is non-NULL, y = x . w^T + residual ([m, n], row stride y_row_stride).
  */
 int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
@@ -130,6 +129,21 @@ int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, c
 int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, const void* w_down,
                   void* h_scratch, void* out, const void* residual, int64_t m, int64_t hidden, int64_t f,
                   int dtype, void* stream);
+
+/*
+ * tk_swiglu_ffn without the scratch argument: the same FFN, with the [m, f]
+ * activation kept in a fixed 8 MiB array inside the library's own device
+ * memory, so the call allocates no device memory. No counterpart in the
+ * reference: it is for callers that cannot allocate - hosts that own all device
+ * memory and pass only inputs and outputs, or loops that must not call
+ * cudaMalloc/cudaFree. Requires m * f * 2 <= 8 MiB (else TK_ERR_INVALID). The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture starts. All calls on a device share the array, so calls that
+ * overlap on the GPU race and must be ordered by the caller.
+ */
+int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
+                          const void* w_down, void* out, const void* residual, int64_t m, int64_t hidden,
+                          int64_t f, int dtype, void* stream);
 
 #ifdef __cplusplus
 }
