@@ -98,3 +98,34 @@ def test_qwen_shaped_two_layers_bf16():
         out = np32(model(tokens.cuda()))
     rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
     assert rel <= 2e-2
+
+
+def test_block_fusion_matches_unfused_and_skips_other_structures():
+    """Fused blocks (residual adds in the GEMM epilogues) equal the leaf-patched blocks;
+    a block with another structure (parallel attention + FFN) is not fused."""
+    require_b200()
+    import torch.nn as nn
+    import tinker_b200
+    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    from tinker_b200.fusion import fuse_decoder_blocks
+    cfg = TINY.with_(num_layers=3)
+    tokens = make_tokens(cfg, 2, 64, seed=9).cuda()
+    a = tinker_b200.optimize(build_model(cfg, seed=4).cuda(), dtype=torch.float16, fuse_blocks=False)
+    b = tinker_b200.optimize(build_model(cfg, seed=4).cuda(), dtype=torch.float16, fuse_blocks=True)
+    assert all(getattr(l, "_tinker_block_parts", None) for l in b.layers)
+    assert not any(getattr(l, "_tinker_block_parts", None) for l in a.layers)
+    with torch.inference_mode():
+        ya, yb = a(tokens).float(), b(tokens).float()
+    assert ((ya - yb).norm() / ya.norm()).item() < 5e-3
+
+    class Parallel(nn.Module):  # x + attn(n1(x)) + ffn(n2(x)): same children, different math
+        def __init__(self, blk):
+            super().__init__()
+            self.attn_norm, self.attn, self.ffn_norm, self.ffn = blk.attn_norm, blk.attn, blk.ffn_norm, blk.ffn
+
+        def forward(self, x):
+            return x + self.attn(self.attn_norm(x)) + self.ffn(self.ffn_norm(x))
+
+    wrapper = nn.Module()
+    wrapper.blk = Parallel(a.layers[0])
+    assert fuse_decoder_blocks(wrapper) == 0

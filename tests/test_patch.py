@@ -98,3 +98,65 @@ def test_no_cpu_fallback():
 
 def test_param_count_of_the_268m_config():
     assert LLAMA_268M.num_params() == 268_473_344
+
+
+def test_block_fusion_candidates_and_signature_rule():
+    from tinker_b200.fusion import _block_parts, _takes_hidden_states_only
+    m = build_model(TINY)
+    tinker_b200.patch_model(m)
+    blk = m.layers[0]
+    assert _block_parts(blk) == ("attn_norm", "attn", "ffn_norm", "ffn")
+    assert _takes_hidden_states_only(blk)
+    assert _block_parts(m) is None
+
+    class TwoArgs(nn.Module):
+        def forward(self, x, mask):
+            return x
+
+    assert not _takes_hidden_states_only(TwoArgs())
+
+
+def test_block_dataflow_check_accepts_prenorm_and_rejects_other_structures():
+    from tinker_b200.fusion import _dataflow_is_prenorm_residual
+
+    class N(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(8))
+
+        def forward(self, x):
+            return x * 1.0
+
+    class L(nn.Module):
+        def forward(self, x):
+            return x * 0.5
+
+    class PreNorm(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.n1, self.a, self.n2, self.f = N(), L(), N(), L()
+
+        def forward(self, x):
+            x = x + self.a(self.n1(x))
+            return x + self.f(self.n2(x))
+
+    class Parallel(PreNorm):
+        def forward(self, x):
+            return x + self.a(self.n1(x)) + self.f(self.n2(x))
+
+    class PostNorm(PreNorm):
+        def forward(self, x):
+            x = self.n1(x + self.a(x))
+            return self.n2(x + self.f(x))
+
+    class Scaled(PreNorm):
+        def forward(self, x):
+            x = x + 0.5 * self.a(self.n1(x))
+            return x + self.f(self.n2(x))
+
+    parts = ("n1", "a", "n2", "f")
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, 4, 8)
+    assert _dataflow_is_prenorm_residual(PreNorm(), parts, x, g)
+    for cls in (Parallel, PostNorm, Scaled):
+        assert not _dataflow_is_prenorm_residual(cls(), parts, x, g), cls.__name__

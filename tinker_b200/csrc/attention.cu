@@ -147,9 +147,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
 
   if (tid == 0) {
+    pdl_launch_dependents();
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
     prefetch_tmap(&tv);
+    pdl_wait();  // q, k, v are written by the previous kernel
     mbar_arrive_expect_tx(kv_full, S::Q_BYTES + S::K_BYTES + S::V_BYTES);
 #pragma unroll
     for (int blk = 0; blk < D / 64; ++blk) {
@@ -322,9 +324,8 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
       return rc;
     configured[dev.device] = true;
   }
-  dim3 grid(p.n_qtiles, p.num_heads, p.batch);
-  kern<<<grid, THREADS, S::TOTAL, st>>>(tq, tk_, tv, p);
-  return check_launch("rope_attention_kernel");
+  return launch_kernel(kern, dim3(p.n_qtiles, p.num_heads, p.batch), dim3(THREADS), S::TOTAL, st, 1,
+                       "rope_attention_kernel", tq, tk_, tv, p);
 }
 
 }  // namespace attn

@@ -18,6 +18,7 @@
 // BN/2 rows of the up weight, so gate and up of one output column sit in the
 // same accumulator tile.
 #include <algorithm>
+#include <cmath>
 #include <numeric>
 
 #include "tk_common.cuh"
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -185,6 +187,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (EPI == EPI_STORE && p.seg2 < p.n_tiles) prefetch_tmap(&tb2);
       const uint64_t pol_w = policy_evict_first();  // weights are streamed once per tile row
       const uint64_t pol_a = policy_evict_last();   // activations are re-read by every n-tile
+      auto load_b = [&](int stage, int nt, int kb) {
+        uint8_t* sb = ring_b + stage * S::B_BYTES;
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_load_2d_hint(sb, &tb0, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+          tma_load_2d_hint(sb + (BN / 2) * 128, &tb1, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
+        }
+      };
+      // The weights do not depend on the previous kernel: fill the ring with the first
+      // tile's weight tiles before waiting for that kernel, and load activations after.
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < total_tiles) {
+        int mt0, nt0;
+        tile_coords(blockIdx.x, p, mt0, nt0);
+        pre = min(STAGES, p.num_kb);
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&full[kb], S::A_BYTES + S::B_BYTES);
+          load_b(kb, nt0, kb);
+        }
+      }
+      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -192,19 +218,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         int mt, nt;
         tile_coords(t, p, mt, nt);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
-          uint8_t* sa = ring_a + stage * S::A_BYTES;
-          uint8_t* sb = ring_b + stage * S::B_BYTES;
-          tma_load_2d_hint(sa, &ta, &full[stage], kb * BK, mt * BM, pol_a);
-          if constexpr (EPI == EPI_SWIGLU) {
-            tma_load_2d_hint(sb, &tb0, &full[stage], kb * BK, nt * (BN / 2), pol_w);
-            tma_load_2d_hint(sb + (BN / 2) * 128, &tb1, &full[stage], kb * BK, nt * (BN / 2), pol_w);
-          } else {
-            const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
-            const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
-            tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
+          if (!(t == static_cast<int>(blockIdx.x) && kb < pre)) {
+            if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
+            load_b(stage, nt, kb);
           }
+          tma_load_2d_hint(ring_a + stage * S::A_BYTES, &ta, &full[stage], kb * BK, mt * BM, pol_a);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -298,6 +317,240 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------
+// Split-K variant for few output tiles (weight streaming at M <= a few hundred).
+//
+// A cluster of `split` CTAs shares one output tile; CTA r of the cluster runs
+// k-blocks [r*num_kb/split, (r+1)*num_kb/split) into its own TMEM accumulator,
+// so each CTA streams 1/split of the activation block and of the weight tile.
+// The partial sums are then reduced through distributed shared memory: the 128
+// rows are owned in groups of 16 (group g -> CTA g % split); every CTA writes
+// the rows it does not own into the owner's receive buffer (st.shared::cluster),
+// and after a cluster barrier each owner adds the partials to its own and runs
+// the epilogue (SwiGLU / residual / store) for its rows.
+// ---------------------------------------------------------------------------------
+template <int BN>
+struct SplitSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int ROW_F = BN + 4;  // padded fp32 row of the receive buffer (no bank conflicts)
+  static constexpr int MAX_STAGES = 8;
+  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  __host__ __device__ static constexpr int rows_owned_max(int split) {
+    return split > 1 ? ((8 + split - 1) / split) * 16 : 0;
+  }
+  __host__ __device__ static constexpr int recv_bytes(int split) {
+    return split > 1 ? (split - 1) * rows_owned_max(split) * ROW_F * 4 : 0;
+  }
+  __host__ __device__ static constexpr int bar_off(int split, int stages) { return stages * STAGE + recv_bytes(split); }
+  __host__ __device__ static constexpr int total(int split, int stages) {
+    return 1024 + bar_off(split, stages) + (2 * MAX_STAGES + 2) * 8 + 16;
+  }
+};
+
+template <int DT, int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_splitk_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+                       const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tb2,
+                       const Params p, const int split, const int stages) {
+  using S = SplitSmem<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  float* recv = reinterpret_cast<float*>(smem + stages * S::STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar_off(split, stages));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S::MAX_STAGES;
+  uint64_t* tfull = bars + 2 * S::MAX_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S::MAX_STAGES + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int nt = blockIdx.y;
+  const int mt = blockIdx.z;
+  const int kb0 = (rank * p.num_kb) / split;
+  const int kb1 = ((rank + 1) * p.num_kb) / split;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  cluster_sync();  // every CTA of the cluster is running before any remote shared-memory write
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb0);
+      if (EPI == EPI_SWIGLU || p.seg1 < p.n_tiles) prefetch_tmap(&tb1);
+      if (EPI == EPI_STORE && p.seg2 < p.n_tiles) prefetch_tmap(&tb2);
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      auto load_b = [&](int stage, int kb) {
+        uint8_t* sb = ring + stage * S::STAGE + S::A_BYTES;
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_load_2d_hint(sb, &tb0, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+          tma_load_2d_hint(sb + (BN / 2) * 128, &tb1, &full[stage], kb * BK, nt * (BN / 2), pol_w);
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
+        }
+      };
+      // weight tiles first (independent of the previous kernel), activations after it completes
+      const int pre = min(stages, kb1 - kb0);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], S::STAGE);
+        load_b(i, kb0 + i);
+      }
+      pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (kb - kb0 >= pre) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) break;
+          mbar_arrive_expect_tx(&full[stage], S::STAGE);
+          load_b(stage, kb);
+        }
+        tma_load_2d_hint(ring + stage * S::STAGE, &ta, &full[stage], kb * BK, mt * BM, pol_a);
+        if (++stage == stages) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(Dt<DT>::umma_fmt, BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(ring + stage * S::STAGE);
+        const uint32_t b0 = a0 + S::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_f16_ss(tmem_base, make_sw128_desc(a0 + kk * 32, 0, 1024), make_sw128_desc(b0 + kk * 32, 0, 1024),
+                      idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == stages) { stage = 0; phase ^= 1; }
+      }
+      if (ok) umma_commit(tfull);
+    }
+  }
+
+  // epilogue warps: send the rows other CTAs own (tcgen05.ld is warp-wide, so a warp
+  // loads whenever any of its lanes needs its row)
+  const int quarter = warp & 3;
+  const int group = quarter * 2 + (lane >> 4);  // 16-row group of this lane's row
+  const int owner = group % split;
+  const int local_row = (group / split) * 16 + (lane & 15);
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+  bool have_acc = false;
+  if (warp >= 2) {
+    have_acc = mbar_wait(tfull, 0);
+    tc_fence_after();
+    if (have_acc && __any_sync(0xffffffffu, owner != rank)) {
+      const int slot = rank < owner ? rank : rank - 1;
+      const uint32_t remote =
+          mapa_shared(smem_u32(recv + (slot * S::rows_owned_max(split) + local_row) * S::ROW_F), owner);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + c, v);
+        tmem_wait_ld();
+        if (owner != rank) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_cluster_v4(remote + (c + 4 * j) * 4, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+      }
+    }
+  }
+  cluster_sync();  // all partials have landed in their owners' receive buffers
+
+  if (warp >= 2 && have_acc && __any_sync(0xffffffffu, owner == rank)) {
+    const bool mine = owner == rank;
+    const int row = mt * BM + quarter * 32 + lane;
+    const float* rbase = recv + local_row * S::ROW_F;
+    const int rstride = S::rows_owned_max(split) * S::ROW_F;
+    if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
+      float g[32], u[16];
+      tmem_ld16(taddr, g);
+      tmem_ld16(taddr + BN / 2, u);
+      tmem_wait_ld();
+      for (int s2 = 0; mine && s2 < split - 1; ++s2) {
+        const float* r = rbase + s2 * rstride;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          g[j] += r[j];
+          u[j] += r[BN / 2 + j];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+      if (mine && row < p.m) store_row16<DT>(p.y, p.ldy, row, nt * (BN / 2), p.n, g);
+    } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 32) {
+        float g[32], u[32];
+        tmem_ld32(taddr + c, g);
+        tmem_ld32(taddr + BN / 2 + c, u);
+        tmem_wait_ld();
+        for (int s2 = 0; mine && s2 < split - 1; ++s2) {
+          const float4* rg = reinterpret_cast<const float4*>(rbase + s2 * rstride + c);
+          const float4* ru = reinterpret_cast<const float4*>(rbase + s2 * rstride + BN / 2 + c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 a = rg[j], b = ru[j];
+            g[4 * j] += a.x; g[4 * j + 1] += a.y; g[4 * j + 2] += a.z; g[4 * j + 3] += a.w;
+            u[4 * j] += b.x; u[4 * j + 1] += b.y; u[4 * j + 2] += b.z; u[4 * j + 3] += b.w;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+        if (mine && row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + c, v);
+        tmem_wait_ld();
+        for (int s2 = 0; mine && s2 < split - 1; ++s2) {
+          const float4* r = reinterpret_cast<const float4*>(rbase + s2 * rstride + c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 a = r[j];
+            v[4 * j] += a.x; v[4 * j + 1] += a.y; v[4 * j + 2] += a.z; v[4 * j + 3] += a.w;
+          }
+        }
+        if (mine && row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------
 template <int DT, int BN, int EPI, int STAGES>
@@ -316,8 +569,82 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = std::max(1, std::min(tiles, dev.sm_count * ctas_per_sm));
-  kern<<<grid, THREADS, S::TOTAL, st>>>(ta, tb0, tb1, tb2, p);
-  return check_launch("gemm_kernel");
+  return launch_kernel(kern, dim3(grid), dim3(THREADS), S::TOTAL, st, 1, "gemm_kernel", ta, tb0, tb1, tb2, p);
+}
+
+template <int DT, int BN, int EPI>
+int launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& tb2,
+                  const Params& p, int split, int stages, cudaStream_t st) {
+  using S = SplitSmem<BN>;
+  auto kern = gemm_splitk_kernel<DT, BN, EPI>;
+  static bool configured[64] = {};
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  if (!configured[dev.device]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(dev.smem_optin)),
+                            "cudaFuncSetAttribute(gemm_splitk)"))
+      return rc;
+    configured[dev.device] = true;
+  }
+  return launch_kernel(kern, dim3(split, p.n_tiles, p.m_tiles), dim3(THREADS), S::total(split, stages), st, split,
+                       "gemm_splitk_kernel", ta, tb0, tb1, tb2, p, split, stages);
+}
+
+// Tile plan for problems with few output tiles: split K over a cluster of `split`
+// CTAs when that keeps all CTAs in one wave and cuts the bytes each CTA must pull.
+struct SmallPlan {
+  int bn = 0, split = 1, stages = 4;
+};
+static int splitk_smem(int bn, int split, int stages) {
+  switch (bn) {
+    case 256: return SplitSmem<256>::total(split, stages);
+    case 128: return SplitSmem<128>::total(split, stages);
+    case 64: return SplitSmem<64>::total(split, stages);
+    default: return SplitSmem<32>::total(split, stages);
+  }
+}
+// Cost model fitted to timestamped runs of both kernels at M = 128 on B200 (µs):
+// ~1.8 of set-up and first-load latency, the CTA's k-slice of activations plus
+// weights at ~100 GB/s per SM, and for split > 1 a DSMEM reduction of
+// ~0.8 + (partial bytes sent) / 25 GB/s; the owner epilogue grows with BN.
+// Splits stay <= 4 (cluster barriers and start-up spread grow beyond that) and
+// BN <= 64 (larger tiles make the reduction dominate).
+static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sms, bool swiglu, int64_t constraint,
+                              size_t smem_cap) {
+  SmallPlan best;
+  double best_cost = 1e30;
+  static const int bns[] = {64, 32};
+  for (int bn : bns) {
+    const int64_t per_tile_n = swiglu ? bn / 2 : bn;
+    if (!swiglu && constraint % bn != 0) continue;
+    const int64_t n_tiles = (n_out + per_tile_n - 1) / per_tile_n;
+    for (int split = 1; split <= 4; ++split) {
+      if (split > num_kb) break;
+      const int64_t ctas = m_tiles * n_tiles * split;
+      if (split > 1 && ctas > sms) continue;  // the split kernel runs in one wave
+      const double kb_per_cta = double(num_kb) / split;
+      const double load = kb_per_cta * (BM * BK * 2 + bn * BK * 2);
+      const double red = split > 1 ? 128.0 * bn * 4 * (split - 1) / split : 0.0;
+      // persistent kernel: CTAs beyond one per SM share SMs
+      const double per_sm = split > 1 ? 1.0 : double((ctas + sms - 1) / sms);
+      const double cost = 1.8 + per_sm * load / 100e3 + (split > 1 ? 0.8 + red / 25e3 : 0.0) + 0.25 * bn / 32;
+      int stages = 0;
+      if (split > 1) {
+        const int want = std::min<int>(SplitSmem<32>::MAX_STAGES, int(std::ceil(kb_per_cta)));
+        for (int s = want; s >= 2; --s)
+          if (static_cast<size_t>(splitk_smem(bn, split, s)) <= smem_cap) { stages = s; break; }
+        if (stages < std::min(want, 3)) continue;
+      }
+      if (cost < best_cost * 0.97) {
+        best_cost = cost;
+        best.bn = bn;
+        best.split = split;
+        best.stages = stages;
+      }
+    }
+  }
+  return best;
 }
 
 // Largest BN (from the candidates) whose tile count still fills the GPU, else the
@@ -344,8 +671,14 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   // all but the last weight block must be whole tiles
   const int64_t constraint = (n1 || n2) ? std::gcd(n0, n1 ? n1 : n0) : 256;
   static const int cands[] = {256, 128, 64, 32};
-  const int bn = pick_bn(m_tiles, n, dev.sm_count, cands, 4, constraint);
+  int bn = pick_bn(m_tiles, n, dev.sm_count, cands, 4, constraint);
   if (bn == 0) return fail_invalid("linear: weight block sizes must be multiples of 32");
+  SmallPlan plan;
+  if (m_tiles * ((n + bn - 1) / bn) < dev.sm_count) {
+    plan = plan_small_m(m_tiles, n, static_cast<int>((k + BK - 1) / BK), dev.sm_count, false, constraint,
+                        dev.smem_optin);
+    if (plan.bn) bn = plan.bn;
+  }
   Params p{};
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
@@ -367,6 +700,14 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
     if (int rc = tensor_map_2d(&tb1, w1, DT, n1, k, k, bn, BK)) return rc;
   if (n2)
     if (int rc = tensor_map_2d(&tb2, w2, DT, n2, k, k, bn, BK)) return rc;
+  if (plan.split > 1) {
+    switch (bn) {
+      case 256: return launch_splitk<DT, 256, EPI_STORE>(ta, tb0, tb1, tb2, p, plan.split, plan.stages, st);
+      case 128: return launch_splitk<DT, 128, EPI_STORE>(ta, tb0, tb1, tb2, p, plan.split, plan.stages, st);
+      case 64: return launch_splitk<DT, 64, EPI_STORE>(ta, tb0, tb1, tb2, p, plan.split, plan.stages, st);
+      default: return launch_splitk<DT, 32, EPI_STORE>(ta, tb0, tb1, tb2, p, plan.split, plan.stages, st);
+    }
+  }
   switch (bn) {
     case 256: return launch<DT, 256, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 1, st);
     case 128: return launch<DT, 128, EPI_STORE, 5>(ta, tb0, tb1, tb2, p, 1, st);
@@ -386,7 +727,13 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
   int half = 0;
   for (int c : cands_half)
     if (m_tiles * ((f + c - 1) / c) >= dev.sm_count) { half = c; break; }
-  if (!half) half = 16;
+  SmallPlan plan;
+  if (!half) {
+    half = 16;
+    plan = plan_small_m(m_tiles, f, static_cast<int>((hidden + BK - 1) / BK), dev.sm_count, true, 1,
+                        dev.smem_optin);
+    if (plan.bn) half = plan.bn / 2;
+  }
   Params p{};
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(f);
@@ -402,6 +749,14 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
   if (int rc = tensor_map_2d(&ta, x, DT, m, hidden, lda, BM, BK)) return rc;
   if (int rc = tensor_map_2d(&tg, wg, DT, f, hidden, hidden, half, BK)) return rc;
   if (int rc = tensor_map_2d(&tu, wu, DT, f, hidden, hidden, half, BK)) return rc;
+  if (plan.split > 1) {
+    switch (half) {
+      case 128: return launch_splitk<DT, 256, EPI_SWIGLU>(ta, tg, tu, tu, p, plan.split, plan.stages, st);
+      case 64: return launch_splitk<DT, 128, EPI_SWIGLU>(ta, tg, tu, tu, p, plan.split, plan.stages, st);
+      case 32: return launch_splitk<DT, 64, EPI_SWIGLU>(ta, tg, tu, tu, p, plan.split, plan.stages, st);
+      default: return launch_splitk<DT, 32, EPI_SWIGLU>(ta, tg, tu, tu, p, plan.split, plan.stages, st);
+    }
+  }
   switch (half) {
     case 128: return launch<DT, 256, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 1, st);
     case 64: return launch<DT, 128, EPI_SWIGLU, 5>(ta, tg, tu, tu, p, 1, st);

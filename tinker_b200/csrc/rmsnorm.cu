@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const void* __restrict
   constexpr int E = V::N;
   constexpr int WARPS = TPR / 32;
   __shared__ float red[256 / 32];
+  pdl_launch_dependents();
+  pdl_wait();  // x (and the residual) are written by earlier kernels
   const int t = threadIdx.x;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
   const bool active = row < rows;
@@ -125,6 +127,8 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const void* __restr
                                                               int wdt, void* y, int64_t ys, void* res_out,
                                                               int64_t rows, int dim, float eps) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   float ss = 0.f;
   for (int c = threadIdx.x; c < dim; c += blockDim.x) {
@@ -161,15 +165,24 @@ int launch_rmsnorm(const void* x, int64_t xs, const void* res, const void* w, in
   const bool vec_ok = dim % E == 0 && (xs * es) % 16 == 0 && (ys * es) % 16 == 0 && aligned16(x) && aligned16(y) &&
                       (!ADD || (aligned16(res) && aligned16(res_out)));
   const int64_t nvec = dim / E;
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
   if (vec_ok && nvec <= 2048) {
 #define TK_RMS_LAUNCH(NV, TPR)                                                                                 \
   {                                                                                                            \
     dim3 block(TPR, TPR >= 128 ? 1 : 128 / TPR);                                                               \
     dim3 grid(static_cast<unsigned>((rows + block.y - 1) / block.y));                                          \
-    rmsnorm_vec_kernel<DT, NV, TPR, ADD><<<grid, block, 0, st>>>(x, xs, res, w, wdt, y, ys, res_out, rows,     \
-                                                                 static_cast<int>(dim), eps);                  \
-    return check_launch("rmsnorm_vec_kernel");                                                                 \
+    return launch_kernel(rmsnorm_vec_kernel<DT, NV, TPR, ADD>, grid, block, 0, st, 1, "rmsnorm_vec_kernel", x, xs, \
+                         res, w, wdt, y, ys, res_out, rows, static_cast<int>(dim), eps);                      \
   }
+    if (rows < 4 * static_cast<int64_t>(dev.sm_count)) {
+      // few rows: one row per block and one vector per thread, to spread a small
+      // problem over as many SMs (and as many loads in flight) as possible
+      if (nvec <= 64) TK_RMS_LAUNCH(1, 64)
+      if (nvec <= 128) TK_RMS_LAUNCH(1, 128)
+      if (nvec <= 256) TK_RMS_LAUNCH(1, 256)
+      if (nvec <= 512) TK_RMS_LAUNCH(2, 256)
+    }
     if (nvec <= 32) TK_RMS_LAUNCH(1, 32)
     if (nvec <= 64) TK_RMS_LAUNCH(2, 32)
     if (nvec <= 128) TK_RMS_LAUNCH(4, 32)
@@ -179,9 +192,8 @@ int launch_rmsnorm(const void* x, int64_t xs, const void* res, const void* w, in
     TK_RMS_LAUNCH(8, 256)
 #undef TK_RMS_LAUNCH
   }
-  rmsnorm_scalar_kernel<DT, ADD><<<static_cast<unsigned>(rows), 256, 0, st>>>(x, xs, res, w, wdt, y, ys, res_out,
-                                                                              rows, static_cast<int>(dim), eps);
-  return check_launch("rmsnorm_scalar_kernel");
+  return launch_kernel(rmsnorm_scalar_kernel<DT, ADD>, dim3(static_cast<unsigned>(rows)), dim3(256), 0, st, 1,
+                       "rmsnorm_scalar_kernel", x, xs, res, w, wdt, y, ys, res_out, rows, static_cast<int>(dim), eps);
 }
 
 template <bool ADD>
@@ -211,6 +223,8 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(const void* __restrict_
   constexpr int E = V::N;
   constexpr int ES = DT == TK_F32 ? 4 : 2;
   const int64_t total = rows * vpr;
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / vpr, c = i - r * vpr;
@@ -228,6 +242,8 @@ __global__ void __launch_bounds__(256) swiglu_scalar_kernel(const void* __restri
                                                              const void* __restrict__ u, int64_t us, void* o,
                                                              int64_t os, int64_t rows, int64_t n) {
   const int64_t total = rows * n;
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / n, c = i - r * n;
@@ -252,13 +268,13 @@ int launch_swiglu(const void* g, int64_t gs, const void* u, int64_t us, void* o,
   if (vec_ok) {
     const int64_t total = rows * (n / E);
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cap, (total + 255) / 256)));
-    swiglu_vec_kernel<DT><<<grid, 256, 0, st>>>(g, gs, u, us, o, os, rows, n / E);
-    return check_launch("swiglu_vec_kernel");
+    return launch_kernel(swiglu_vec_kernel<DT>, dim3(grid), dim3(256), 0, st, 1, "swiglu_vec_kernel", g, gs, u, us,
+                         o, os, rows, n / E);
   }
   const int64_t total = rows * n;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cap, (total + 255) / 256)));
-  swiglu_scalar_kernel<DT><<<grid, 256, 0, st>>>(g, gs, u, us, o, os, rows, n);
-  return check_launch("swiglu_scalar_kernel");
+  return launch_kernel(swiglu_scalar_kernel<DT>, dim3(grid), dim3(256), 0, st, 1, "swiglu_scalar_kernel", g, gs, u,
+                       us, o, os, rows, n);
 }
 
 }  // namespace

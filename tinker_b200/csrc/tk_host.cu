@@ -1,6 +1,7 @@
 // Host runtime of the library: error reporting, device queries, tensor maps,
 // and the small entry points (version, device check, device error word).
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -23,6 +24,14 @@ int set_error(int code, const std::string& msg) {
 int check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return TK_OK;
   return set_error(TK_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TINKER_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int current_device_info(DeviceInfo* out) {

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/tinker_b200.h"
 
@@ -36,6 +37,40 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline int elem_size(int dt) { return dt == TK_F32 ? 4 : 2; }
 inline bool valid_dtype(int dt) { return dt == TK_F16 || dt == TK_BF16 || dt == TK_F32; }
 inline bool half_dtype(int dt) { return dt == TK_F16 || dt == TK_BF16; }
+
+// Programmatic dependent launch on (default) or off (TINKER_B200_PDL=0 in the environment).
+bool pdl_enabled();
+
+// Launch `kern` with cudaLaunchKernelEx: programmatic stream serialisation when
+// PDL is enabled (the kernel overlaps its set-up with the previous kernel and
+// orders its dependent reads with griddepcontrol.wait), and a cluster of
+// `cluster_x` CTAs along x when cluster_x > 1.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+                  const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
 
 // 2-D tensor map over a row-major [rows, cols] matrix of 2-byte elements
 // (row stride in elements), box [box_rows, box_cols], 128-byte swizzle.

@@ -1,0 +1,123 @@
+"""Decoder-block fusion: the residual adds move into the GEMM epilogues.
+
+The reference patches leaf modules only (tinker/patch.py:57-116), so each
+pre-norm block still runs ``x = x + attn(norm1(x)); x = x + ffn(norm2(x))``
+with two separate elementwise adds in user code. After leaf patching, a block
+whose children are exactly a ``TinKerRMSNorm``, a ``TinKerAttention``, a
+``TinKerRMSNorm`` and a ``TinKerSwiGLU`` (any attribute names, in that order)
+and whose ``forward`` takes the hidden states alone is a candidate: its forward
+is replaced by
+
+    h = attn(norm1(x), residual=x)      # o_proj epilogue adds x
+    y = ffn(norm2(h), residual=h)       # down_proj epilogue adds h
+
+which is 7 kernels per block and no torch kernel in between. The replacement is
+bound only after the block's own forward is shown to have exactly that
+dataflow: forward hooks substitute large random tensors for the outputs of the
+four children and record their inputs, and the block must feed ``x`` to norm1,
+norm1's output to attn, ``x + attn`` to norm2, norm2's output to ffn, call each
+once, and return ``x + attn + ffn``. Blocks with any other structure (parallel
+attention/FFN, post-norm, scaled residuals) are left as they are.
+"""
+
+from __future__ import annotations
+
+import inspect
+import types
+
+import torch
+import torch.nn as nn
+
+from tinker_b200.modules.attention import TinKerAttention
+from tinker_b200.modules.feed_forward import TinKerSwiGLU
+from tinker_b200.modules.normalization import TinKerRMSNorm
+
+_PATTERN = (TinKerRMSNorm, TinKerAttention, TinKerRMSNorm, TinKerSwiGLU)
+
+
+def _block_parts(block: nn.Module):
+    kids = list(block.named_children())
+    if len(kids) != 4 or tuple(type(m) for _, m in kids) != _PATTERN:
+        return None
+    return tuple(n for n, _ in kids)
+
+
+def _takes_hidden_states_only(block: nn.Module) -> bool:
+    try:
+        sig = inspect.signature(block.forward)
+    except (TypeError, ValueError):
+        return False
+    required = [p for p in sig.parameters.values()
+                if p.default is inspect.Parameter.empty
+                and p.kind in (inspect.Parameter.POSITIONAL_ONLY, inspect.Parameter.POSITIONAL_OR_KEYWORD)]
+    return len(required) == 1
+
+
+def _fused_forward(self, x: torch.Tensor) -> torch.Tensor:
+    n1, at, n2, ff = self._tinker_block_parts
+    h = getattr(self, at)(getattr(self, n1)(x), residual=x)
+    return getattr(self, ff)(getattr(self, n2)(h), residual=h)
+
+
+def _dataflow_is_prenorm_residual(block: nn.Module, parts, x: torch.Tensor, gen) -> bool:
+    """Run the block's own forward with its children's outputs replaced by known
+    tensors and check the pre-norm residual dataflow (see the module docstring)."""
+    mods = [getattr(block, n) for n in parts]
+    subst = [torch.randn(x.shape, device=x.device, generator=gen).to(x.dtype) * 4.0 for _ in mods]
+    seen = [[] for _ in mods]
+    handles = []
+    for i, m in enumerate(mods):
+        handles.append(m.register_forward_pre_hook(lambda mod, args, i=i: seen[i].append(args[0] if args else None)))
+        handles.append(m.register_forward_hook(lambda mod, args, out, i=i: subst[i]))
+    try:
+        with torch.inference_mode():
+            out = block(x)
+    finally:
+        for h in handles:
+            h.remove()
+    if any(len(v) != 1 or v[0] is None for v in seen):
+        return False
+    n1, a, n2, f = subst
+    h = x + a
+    checks = [(seen[0][0], x), (seen[1][0], n1), (seen[2][0], h), (seen[3][0], n2), (out, h + f)]
+    for got, want in checks:
+        if not isinstance(got, torch.Tensor) or got.shape != want.shape:
+            return False
+        if not torch.allclose(got.float(), want.float(), rtol=1e-2, atol=1e-2):
+            return False
+    return True
+
+
+def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: int = 16) -> int:
+    """Give every qualifying pre-norm decoder block the fused forward; returns how many."""
+    fused = 0
+    gen = None
+    for name, block in model.named_modules():
+        parts = _block_parts(block)
+        if parts is None or getattr(block, "_tinker_block_parts", None) is not None:
+            continue
+        if not _takes_hidden_states_only(block):
+            if verbose:
+                print(f"  [tinker] block {name}: forward takes more than the hidden states, not fused")
+            continue
+        norm1 = getattr(block, parts[0])
+        w = getattr(block, parts[1]).q_proj.weight
+        if gen is None:
+            gen = torch.Generator(device=w.device).manual_seed(1234)
+        x = torch.randn(1, probe_tokens, norm1.weight.shape[0], device=w.device, generator=gen).to(w.dtype)
+        try:
+            ok = _dataflow_is_prenorm_residual(block, parts, x, gen)
+        except Exception as e:  # a block whose forward cannot run on the probe keeps its own forward
+            ok = False
+            if verbose:
+                print(f"  [tinker] block {name}: not fused ({e})")
+        if not ok:
+            if verbose:
+                print(f"  [tinker] block {name}: not a pre-norm residual block, not fused")
+            continue
+        block._tinker_block_parts = parts
+        block.forward = types.MethodType(_fused_forward, block)
+        fused += 1
+        if verbose:
+            print(f"  [tinker] fused decoder block {name}")
+    return fused

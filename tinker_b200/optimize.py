@@ -4,7 +4,7 @@
   1. module patching: RMSNorm / SwiGLU FFN / GQA attention -> ``TinKer*`` modules
      running the sm_100a kernels (the reference gates this on Triton being
      importable; here it needs the built kernel library and a B200)
-  2. half precision (``dtype``)
+  2. half precision (``dtype``), then decoder-block fusion (``fuse_blocks``)
   3. int8 dynamic quantization: not part of the B200 path (the reference's is a
      CPU-only ``quantize_dynamic``); reported and skipped
   4. ``compile``: accepted and not used - the patched forward already runs
@@ -19,6 +19,7 @@ import torch
 import torch.nn as nn
 
 from tinker_b200 import _lib
+from tinker_b200.fusion import fuse_decoder_blocks
 from tinker_b200.patch import patch_model
 
 
@@ -38,12 +39,16 @@ def optimize(
     graph_vocab_size: int = 32000,
     verbose: bool = False,
     graph_clone_output: bool = True,
+    fuse_blocks: bool = True,
 ) -> nn.Module:
     """optimize a model for inference on a B200.
 
-    Same arguments as the reference. ``graph_clone_output`` (extra, default True
-    as in the reference) controls whether the CUDA-graph wrapper returns a clone
-    of its static output or the static output itself.
+    Same arguments as the reference, plus two:
+    ``graph_clone_output`` (default True, as in the reference) controls whether the
+    CUDA-graph wrapper returns a clone of its static output or the static output
+    itself; ``fuse_blocks`` (default True) gives qualifying pre-norm decoder blocks
+    a forward whose residual adds run inside the GEMM epilogues
+    (``tinker_b200.fusion``), after checking the block's dataflow.
     """
     model.eval()
     params = list(model.parameters())
@@ -68,6 +73,11 @@ def optimize(
         if verbose:
             print(f"  [tinker] casting to {dtype}")
         model = model.to(dtype=dtype)
+
+    if fuse_blocks and replace_attention and replace_ffn and replace_norm:
+        n = fuse_decoder_blocks(model, verbose=verbose)
+        if verbose:
+            print(f"  [tinker] fused {n} decoder blocks (residual adds in the GEMM epilogues)")
 
     if quantize and verbose:
         print("  [tinker] int8 quantization skipped: not part of the B200 kernel path")
