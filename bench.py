@@ -268,13 +268,13 @@ def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
     return {
         "gate_up_swiglu": ([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight)
                             for l in layers], 2 * F * H * es + M * H * es + M * F * es, 2 * M * H * 2 * F, len(layers)),
-        "down_proj": ([lambda l=l: linear(hbuf, l.ffn.down_proj.weight) for l in layers],
-                      H * F * es + M * F * es + M * H * es, 2 * M * F * H, len(layers)),
+        "down_proj": ([lambda l=l: linear(hbuf, l.ffn.down_proj.weight, residual=x) for l in layers],
+                      H * F * es + M * F * es + 2 * M * H * es, 2 * M * F * H, len(layers)),
         "qkv_proj": ([lambda l=l: linear(x, l.attn.q_proj.weight, l.attn.k_proj.weight, l.attn.v_proj.weight)
                       for l in layers], (hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es,
                      2 * M * H * (hq + 2 * hkv) * D, len(layers)),
-        "o_proj": ([lambda l=l: linear(a, l.attn.o_proj.weight) for l in layers],
-                   H * hq * D * es + M * hq * D * es + M * H * es, 2 * M * hq * D * H, len(layers)),
+        "o_proj": ([lambda l=l: linear(a, l.attn.o_proj.weight, residual=x) for l in layers],
+                   H * hq * D * es + M * hq * D * es + 2 * M * H * es, 2 * M * hq * D * H, len(layers)),
         "rope_attention": ([lambda: fused_attention(qkv[..., :hq * D], qkv[..., hq * D:(hq + hkv) * D],
                                                     qkv[..., (hq + hkv) * D:], att.cos_table, att.sin_table,
                                                     hq, hkv, D) for _ in layers],

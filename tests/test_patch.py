@@ -160,3 +160,13 @@ def test_block_dataflow_check_accepts_prenorm_and_rejects_other_structures():
     assert _dataflow_is_prenorm_residual(PreNorm(), parts, x, g)
     for cls in (Parallel, PostNorm, Scaled):
         assert not _dataflow_is_prenorm_residual(cls(), parts, x, g), cls.__name__
+
+
+def test_rope_tables_are_shared_across_layers():
+    from tinker_b200.fusion import share_rope_tables
+    m = build_model(TINY.with_(num_layers=3))
+    tinker_b200.patch_model(m)
+    assert share_rope_tables(m) == 2
+    assert m.layers[0].attn.cos_table is m.layers[2].attn.cos_table
+    m.to(torch.float16)
+    assert m.layers[1].attn.sin_table.dtype == torch.float32

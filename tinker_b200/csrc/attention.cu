@@ -145,6 +145,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t t_s = tmem_base;
   const uint32_t t_o = tmem_base + 128;
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  {
+    // the RoPE table rows this thread rotates with (Q row, first K row) do not depend
+    // on the previous kernel: start pulling them into L1 while it finishes
+    const int es = p.table_dtype == TK_F32 ? 4 : 2;
+    const int row_bytes = (D / 2) * es;
+    const int64_t qpos = static_cast<int64_t>(p.start_pos) + q0 + tid;
+    const int64_t kpos = static_cast<int64_t>(p.start_pos) + tid;
+    if (q0 + tid < p.seq && qpos < p.table_rows)
+      for (int b = 0; b < row_bytes; b += 128) {
+        prefetch_l1(static_cast<const char*>(p.cos_t) + qpos * row_bytes + b);
+        prefetch_l1(static_cast<const char*>(p.sin_t) + qpos * row_bytes + b);
+      }
+    if (tid < p.seq && kpos < p.table_rows)
+      for (int b = 0; b < row_bytes; b += 128) {
+        prefetch_l1(static_cast<const char*>(p.cos_t) + kpos * row_bytes + b);
+        prefetch_l1(static_cast<const char*>(p.sin_t) + kpos * row_bytes + b);
+      }
+  }
 
   if (tid == 0) {
     pdl_launch_dependents();

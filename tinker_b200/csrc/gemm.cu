@@ -19,7 +19,10 @@
 // same accumulator tile.
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
 #include <numeric>
+#include <tuple>
 
 #include "tk_common.cuh"
 #include "tk_host.h"
@@ -604,14 +607,55 @@ static int splitk_smem(int bn, int split, int stages) {
     default: return SplitSmem<32>::total(split, stages);
   }
 }
+// How many clusters of `split` CTAs of the split-K kernel can be resident at once
+// with `smem` bytes of shared memory each (queried once per configuration).
+template <int DT, int EPI>
+static int max_active_clusters(int bn, int split, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, int> cache;
+  DeviceInfo dev;
+  if (current_device_info(&dev)) return 0;
+  const auto key = std::make_tuple(dev.device, bn, split, smem);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params, int, int) =
+      bn == 64 ? gemm_splitk_kernel<DT, 64, EPI> : gemm_splitk_kernel<DT, 32, EPI>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dev.smem_optin)) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(split, 1, 1);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = split;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
 // Cost model fitted to timestamped runs of both kernels at M = 128 on B200 (µs):
 // ~1.8 of set-up and first-load latency, the CTA's k-slice of activations plus
-// weights at ~100 GB/s per SM, and for split > 1 a DSMEM reduction of
-// ~0.8 + (partial bytes sent) / 25 GB/s; the owner epilogue grows with BN.
-// Splits stay <= 4 (cluster barriers and start-up spread grow beyond that) and
-// BN <= 64 (larger tiles make the reduction dominate).
-static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sms, bool swiglu, int64_t constraint,
+// weights at ~100 GB/s per SM (shared by the CTAs an SM holds), and for split > 1
+// a DSMEM reduction of ~0.8 + (partial bytes sent) / 25 GB/s; the owner epilogue
+// grows with BN. Split-K plans must fit in one wave of co-resident clusters;
+// rings are kept at <= 4 stages so that two CTAs can share an SM. Splits stay
+// <= 4 and BN <= 64 (beyond that the reduction and cluster barriers dominate).
+template <int DT, int EPI>
+static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sms, int64_t constraint,
                               size_t smem_cap) {
+  constexpr bool swiglu = EPI == EPI_SWIGLU;
   SmallPlan best;
   double best_cost = 1e30;
   static const int bns[] = {64, 32};
@@ -622,20 +666,20 @@ static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sm
     for (int split = 1; split <= 4; ++split) {
       if (split > num_kb) break;
       const int64_t ctas = m_tiles * n_tiles * split;
-      if (split > 1 && ctas > sms) continue;  // the split kernel runs in one wave
       const double kb_per_cta = double(num_kb) / split;
-      const double load = kb_per_cta * (BM * BK * 2 + bn * BK * 2);
-      const double red = split > 1 ? 128.0 * bn * 4 * (split - 1) / split : 0.0;
-      // persistent kernel: CTAs beyond one per SM share SMs
-      const double per_sm = split > 1 ? 1.0 : double((ctas + sms - 1) / sms);
-      const double cost = 1.8 + per_sm * load / 100e3 + (split > 1 ? 0.8 + red / 25e3 : 0.0) + 0.25 * bn / 32;
       int stages = 0;
       if (split > 1) {
-        const int want = std::min<int>(SplitSmem<32>::MAX_STAGES, int(std::ceil(kb_per_cta)));
+        const int want = std::min<int>(4, int(std::ceil(kb_per_cta)));
         for (int s = want; s >= 2; --s)
           if (static_cast<size_t>(splitk_smem(bn, split, s)) <= smem_cap) { stages = s; break; }
         if (stages < std::min(want, 3)) continue;
+        const int clusters = max_active_clusters<DT, EPI>(bn, split, splitk_smem(bn, split, stages));
+        if (m_tiles * n_tiles > clusters) continue;  // the split kernel must run in one wave
       }
+      const double load = kb_per_cta * (BM * BK * 2 + bn * BK * 2);
+      const double red = split > 1 ? 128.0 * bn * 4 * (split - 1) / split : 0.0;
+      const double per_sm = split > 1 ? std::max(1.0, double(ctas) / sms) : double((ctas + sms - 1) / sms);
+      const double cost = 1.8 + per_sm * load / 100e3 + (split > 1 ? 0.8 + red / 25e3 : 0.0) + 0.25 * bn / 32;
       if (cost < best_cost * 0.97) {
         best_cost = cost;
         best.bn = bn;
@@ -674,9 +718,9 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   int bn = pick_bn(m_tiles, n, dev.sm_count, cands, 4, constraint);
   if (bn == 0) return fail_invalid("linear: weight block sizes must be multiples of 32");
   SmallPlan plan;
-  if (m_tiles * ((n + bn - 1) / bn) < dev.sm_count) {
-    plan = plan_small_m(m_tiles, n, static_cast<int>((k + BK - 1) / BK), dev.sm_count, false, constraint,
-                        dev.smem_optin);
+  if (m_tiles <= 2 || m_tiles * ((n + bn - 1) / bn) < dev.sm_count) {
+    plan = plan_small_m<DT, EPI_STORE>(m_tiles, n, static_cast<int>((k + BK - 1) / BK), dev.sm_count, constraint,
+                                       dev.smem_optin);
     if (plan.bn) bn = plan.bn;
   }
   Params p{};
@@ -728,10 +772,10 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
   for (int c : cands_half)
     if (m_tiles * ((f + c - 1) / c) >= dev.sm_count) { half = c; break; }
   SmallPlan plan;
-  if (!half) {
-    half = 16;
-    plan = plan_small_m(m_tiles, f, static_cast<int>((hidden + BK - 1) / BK), dev.sm_count, true, 1,
-                        dev.smem_optin);
+  if (!half) half = 16;
+  if (m_tiles <= 2 || m_tiles * ((f + half - 1) / half) < dev.sm_count) {
+    plan = plan_small_m<DT, EPI_SWIGLU>(m_tiles, f, static_cast<int>((hidden + BK - 1) / BK), dev.sm_count, 1,
+                                        dev.smem_optin);
     if (plan.bn) half = plan.bn / 2;
   }
   Params p{};

@@ -121,3 +121,25 @@ def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: i
         if verbose:
             print(f"  [tinker] fused decoder block {name}")
     return fused
+
+
+def share_rope_tables(model: nn.Module) -> int:
+    """Point every ``TinKerAttention`` with the same table shape, device and values at one
+    cos/sin pair, so the attention kernels of all layers read one L2-resident copy.
+    Returns the number of modules re-pointed."""
+    shared: dict = {}
+    n = 0
+    for m in model.modules():
+        if not isinstance(m, TinKerAttention):
+            continue
+        c, s_ = m.cos_table, m.sin_table
+        key = (tuple(c.shape), c.dtype, c.device, float(m.rope_theta))
+        if key not in shared:
+            shared[key] = (c, s_)
+            continue
+        c0, s0 = shared[key]
+        if c0 is c or not (torch.equal(c0, c) and torch.equal(s0, s_)):
+            continue
+        m.cos_table, m.sin_table = c0, s0
+        n += 1
+    return n

@@ -19,7 +19,7 @@ import torch
 import torch.nn as nn
 
 from tinker_b200 import _lib
-from tinker_b200.fusion import fuse_decoder_blocks
+from tinker_b200.fusion import fuse_decoder_blocks, share_rope_tables
 from tinker_b200.patch import patch_model
 
 
@@ -73,6 +73,9 @@ def optimize(
         if verbose:
             print(f"  [tinker] casting to {dtype}")
         model = model.to(dtype=dtype)
+
+    if replace_attention:
+        share_rope_tables(model)
 
     if fuse_blocks and replace_attention and replace_ffn and replace_norm:
         n = fuse_decoder_blocks(model, verbose=verbose)
