@@ -285,30 +285,45 @@ def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
 
 
 def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
-    """Time each kernel kind standalone on the model's own weights, L2 flushed (by reading a
-    buffer larger than L2) before every launch; return (per-kind table, roofline of the
-    kind with the largest share of the forward)."""
+    """Time each kernel kind on the model's own weights inside a CUDA graph, cold: graph
+    A = [L2 flush, launch] per layer, graph B = [L2 flush] per layer; the kernel's time is
+    (A - B) / layers, CUDA events around the replays. The flush reads a buffer larger than
+    L2. Returns (per-kind table, roofline of the kind with the largest share of the forward)."""
     import torch
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
     flush.zero_()
     sink = torch.empty((), dtype=torch.float32, device=dev)
 
-    def timed(fn_list):
-        ts = []
-        for fn in fn_list:
-            torch.sum(flush, out=sink)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            ts.append((e0, e1))
+    def graph_of(fns):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for fn in fns:
+                torch.sum(flush, dim=0, out=sink)
+                if fn is not None:
+                    fn()
+        return g
+
+    def time_graph(g, reps=5):
+        g.replay()
         torch.cuda.synchronize()
-        return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ts) * 1e-3  # seconds
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e-3  # seconds
 
     kinds = {}
-    for name, (fns, nbytes, flops, per_fwd) in _kernel_cases(model, cfg, dev, tokens_per_fwd).items():
-        timed(fns[:2])  # first-launch set-up (kernel attributes, tensor maps)
-        kinds[name] = dict(t=timed(fns), bytes=nbytes, flops=flops, per_fwd=per_fwd)
+    cases = _kernel_cases(model, cfg, dev, tokens_per_fwd)
+    for name, (fns, nbytes, flops, per_fwd) in cases.items():
+        for fn in fns[:2]:
+            fn()  # first-launch set-up (kernel attributes, tensor maps) outside the capture
+        torch.cuda.synchronize()
+        ga, gb = graph_of(fns), graph_of([None] * len(fns))
+        t = max(1e-9, (time_graph(ga) - time_graph(gb)) / len(fns))
+        del ga, gb
+        kinds[name] = dict(t=t, bytes=nbytes, flops=flops, per_fwd=per_fwd)
     table = {}
     for k, v in kinds.items():
         table[k] = {"us": round(v["t"] * 1e6, 2), "launches_per_fwd": v["per_fwd"],
@@ -325,7 +340,8 @@ def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
             traffic = json.load(f).get(f"llama268m-b1s128/{top}")
     roof = {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
             "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic,
-            "bytes_per_launch": v["bytes"], "note": f"peak {peak_note} (burst copy); launch timed alone, L2 flushed"}
+            "bytes_per_launch": v["bytes"],
+            "note": f"peak {peak_note} (burst copy); per launch in a CUDA graph after an L2 flush (cold)"}
     return table, roof
 
 
@@ -375,12 +391,14 @@ def run_ours(args):
 
     # ---- build + capture ---------------------------------------------------------------
     cpu_model = build_model(cfg, seed=0)
-    n0 = _lib.launch_counter[0]
     model = tinker_b200.optimize(cpu_model.to(dev), dtype=torch.float16, cuda_graph=True,
                                  graph_input_shape=(1, 128), graph_vocab_size=cfg.vocab_size)
     if type(model).__name__ != "_CUDAGraphWrapper":
         raise RuntimeError("CUDA graph capture failed")
-    launches_per_fwd = (_lib.launch_counter[0] - n0) // 4  # 3 warm-up forwards + the captured one
+    with torch.inference_mode():  # count this library's kernels in one forward (the graph holds the same)
+        n0 = _lib.launch_counter[0]
+        model._model(tokens.to(dev))
+        launches_per_fwd = _lib.launch_counter[0] - n0
     model._static_input.copy_(tokens.to(dev))
     graph = model._graph
     sampler = ClockSampler(_gpu_id(dev))

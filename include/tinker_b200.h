@@ -17,6 +17,14 @@
 
 #include <stdint.h>
 
+/* Every entry point is exported; everything else in the library is hidden, so
+ * that its CUDA registration symbols cannot interpose with another library's. */
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -33,18 +41,18 @@ extern "C" {
 #define TK_ERR_UNSUPPORTED 3 /* not an sm_100 device, or a size the kernels do not cover */
 
 /* Library version (major*10000 + minor*100 + patch). */
-int tk_version(void);
+TK_API int tk_version(void);
 
 /* Message for the last non-TK_OK return on this thread ("" if none). */
-const char* tk_last_error(void);
+TK_API const char* tk_last_error(void);
 
 /* TK_OK if `device` is an sm_100 (B200-class) GPU the kernels were built for. */
-int tk_check_device(int device);
+TK_API int tk_check_device(int device);
 
 /* Read (and optionally clear) the sticky device-side error word of the current
  * device. Non-zero means a kernel's bounded wait gave up (1 = timeout) and its
  * outputs are invalid. Synchronises the device; meant for tests and debugging. */
-int tk_device_error(int* code, int clear);
+TK_API int tk_device_error(int* code, int clear);
 
 /*
  * RMSNorm over the last axis: y = x * rsqrt(mean(x^2) + eps) * weight, float32
@@ -54,7 +62,7 @@ int tk_device_error(int* code, int clear);
  * x, y: [rows, dim] with row strides in elements; weight: [dim] of `w_dtype`.
  * dtype, w_dtype in {TK_F16, TK_BF16, TK_F32}.
  */
-int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int w_dtype, void* y,
+TK_API int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int w_dtype, void* y,
                int64_t y_row_stride, int64_t rows, int64_t dim, float eps, int dtype, void* stream);
 
 /*
@@ -64,7 +72,7 @@ int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int w_dt
  * (tinker/kernels/fused_rmsnorm.py:70). All tensors contiguous [rows, dim].
  * residual_out may alias x or residual.
  */
-int tk_add_rmsnorm(const void* x, const void* residual, const void* weight, int w_dtype, void* y,
+TK_API int tk_add_rmsnorm(const void* x, const void* residual, const void* weight, int w_dtype, void* y,
                    void* residual_out, int64_t rows, int64_t dim, float eps, int dtype, void* stream);
 
 /*
@@ -73,7 +81,7 @@ int tk_add_rmsnorm(const void* x, const void* residual, const void* weight, int 
  * (tinker/kernels/fused_swiglu.py:61-66, :47-54, :13-44).
  * gate, up, out: [rows, n] with row strides in elements; dtype in {F16, BF16, F32}.
  */
-int tk_swiglu(const void* gate, int64_t gate_row_stride, const void* up, int64_t up_row_stride, void* out,
+TK_API int tk_swiglu(const void* gate, int64_t gate_row_stride, const void* up, int64_t up_row_stride, void* out,
               int64_t out_row_stride, int64_t rows, int64_t n, int dtype, void* stream);
 
 /*
@@ -88,7 +96,7 @@ int tk_swiglu(const void* gate, int64_t gate_row_stride, const void* up, int64_t
  * `table_dtype`; softmax scale 1/sqrt(head_dim); query head h reads KV head
  * h / (num_heads / num_kv_heads). dtype in {F16, BF16}; head_dim in {64, 128}.
  */
-int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride, const void* v,
+TK_API int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride, const void* v,
                       int64_t v_tok_stride, const void* cos_table, const void* sin_table, int table_dtype,
                       int64_t table_rows, void* out, int64_t out_tok_stride, int batch, int seq, int num_heads,
                       int num_kv_heads, int head_dim, int start_pos, int dtype, void* stream);
@@ -104,7 +112,7 @@ int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k, int64_
  * k and the strides must be multiples of 8; n0, n1 multiples of 32.
  * If residual is non-NULL, y = x . w^T + residual ([m, n], row stride y_row_stride).
  */
-int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
+TK_API int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
               const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
               int64_t k, int dtype, void* stream);
 
@@ -116,7 +124,7 @@ int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, c
  * x: [m, hidden] (row stride x_row_stride), w_gate, w_up: [f, hidden]
  * contiguous, h: [m, f] contiguous. f multiple of 32, hidden multiple of 8.
  */
-int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
+TK_API int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
                       int64_t m, int64_t hidden, int64_t f, int dtype, void* stream);
 
 /*
@@ -126,7 +134,7 @@ int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, c
  * activation between the two GEMMs. out: [m, hidden] contiguous; residual NULL
  * or [m, hidden] contiguous (may alias out).
  */
-int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, const void* w_down,
+TK_API int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, const void* w_down,
                   void* h_scratch, void* out, const void* residual, int64_t m, int64_t hidden, int64_t f,
                   int dtype, void* stream);
 
@@ -141,7 +149,7 @@ int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const
  * stream capture starts. All calls on a device share the array, so calls that
  * overlap on the GPU race and must be ordered by the caller.
  */
-int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
+TK_API int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
                           const void* w_down, void* out, const void* residual, int64_t m, int64_t hidden,
                           int64_t f, int dtype, void* stream);
 

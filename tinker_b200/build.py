@@ -3,7 +3,8 @@
     python -m tinker_b200.build [--force] [--verbose]
 
 Compiles every ``csrc/*.cu`` for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``)
-with relocatable device code, links them into ``tinker_b200/libtinker_b200.so``
+with relocatable device code and hidden symbol visibility (only the ``tk_*`` C ABI
+is exported), links them into ``tinker_b200/libtinker_b200.so``
 against the shared CUDA runtime (the one PyTorch already loaded), and skips the
 work when no source is newer than the library.
 """
@@ -25,7 +26,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libtinker_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC,-O3",
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC,-O3,-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I", INCLUDE]
 
 
@@ -74,7 +75,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, _sources()))
     tmp = LIB + ".tmp"
-    cmd = [nvcc, *ARCH, "-shared", "-rdc=true", "-cudart", "shared", "-o", tmp, *objs]
+    cmd = [nvcc, *ARCH, "-shared", "-rdc=true", "-cudart", "shared", "-Xcompiler", "-fvisibility=hidden", "-o", tmp,
+           *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)
