@@ -115,3 +115,52 @@ def test_linear_rejects_bad_arguments():
         linear(x, w)
     with pytest.raises(TypeError):
         linear(x.float(), w.float())
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("hq, hkv", [(896, 128), (1024, 256)])
+def test_pair_tiles_three_weight_blocks(dt, hq, hkv):
+    """Large M runs 256-row tiles on CTA pairs (tcgen05 cta_group::2)."""
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    torch.manual_seed(hq + hkv)
+    m, k = 4096, 896
+    x = torch.randn(m, k, device="cuda").to(dtype)
+    wq = (0.02 * torch.randn(hq, k, device="cuda")).to(dtype)
+    wk = (0.02 * torch.randn(hkv, k, device="cuda")).to(dtype)
+    wv = (0.02 * torch.randn(hkv, k, device="cuda")).to(dtype)
+    y = linear(x, wq, wk, wv)
+    idx = torch.arange(0, m, 5, device="cuda")  # float64 host reference on a row sample
+    assert rel_err(np32(y[idx]), _ref(x[idx], [wq, wk, wv])) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_pair_tiles_residual_and_ragged_m(dt):
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    torch.manual_seed(3)
+    m, n, k = 8000, 1024, 2816  # 8000 rows: the last 256-row tile is partial
+    x = torch.randn(m, k, device="cuda").to(dtype)
+    w = (0.02 * torch.randn(n, k, device="cuda")).to(dtype)
+    r = torch.randn(m, n, device="cuda").to(dtype)
+    y = linear(x, w, residual=r)
+    idx = torch.cat([torch.arange(0, m, 37, device="cuda"), torch.arange(m - 70, m, device="cuda")])
+    assert rel_err(np32(y[idx]), _ref(x[idx], [w], r[idx])) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_pair_tiles_swiglu(dt):
+    require_b200()
+    from tinker_b200.kernels import gate_up_swiglu
+    dtype = DTYPES[dt]
+    torch.manual_seed(4)
+    m, hidden, f = 4608, 896, 4864
+    x = torch.randn(m, hidden, device="cuda").to(dtype)
+    wg = (0.02 * torch.randn(f, hidden, device="cuda")).to(dtype)
+    wu = (0.02 * torch.randn(f, hidden, device="cuda")).to(dtype)
+    h = gate_up_swiglu(x, wg, wu)
+    idx = torch.arange(0, m, 11, device="cuda")
+    a, b = _ref(x[idx], [wg]), _ref(x[idx], [wu])
+    assert rel_err(np32(h[idx]), a / (1 + np.exp(-a)) * b) <= TOL[dtype]

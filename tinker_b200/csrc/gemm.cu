@@ -320,6 +320,201 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------
+// 2-SM variant for large problems: a cluster of two CTAs (a pair) computes one
+// 256 x BN output tile with tcgen05.mma.cta_group::2. Each CTA holds 128 rows of
+// the A tile and BN/2 rows of the B tile in its own shared memory, so per flop a
+// CTA pulls 2/3 of the operand bytes a 1-SM 128 x BN tile needs - the 1-SM kernel
+// is bound by L2->SM bandwidth at large M. Both CTAs' TMA loads count on the
+// leader's full barrier; the leader's single MMA thread commits to barriers in
+// both CTAs (multicast commit); each CTA's epilogue drains its own 128 TMEM lanes
+// and both release the accumulator on the leader's barrier. For the SwiGLU
+// epilogue rank 0 loads the gate rows and rank 1 the matching up rows, so every
+// accumulator holds gate in columns [0, BN/2) and up in [BN/2, BN).
+// ---------------------------------------------------------------------------------
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int RING = STAGES * STAGE;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;
+  static constexpr int TOTAL = 1024 + RING + NUM_BARS * 8 + 16;
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+};
+
+constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;  // shared::cluster address of the same offset in the pair leader
+
+template <int DT, int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+                     const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tb2, const Params p) {
+  using S = PairSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::RING);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NUM_BARS);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_ctarank());  // 0: leader, 1: follower
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int total_tiles = p.m_tiles * p.n_tiles;  // m_tiles counts 256-row tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // four epilogue warps in each CTA of the pair
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA signal
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb0);
+      if (EPI == EPI_SWIGLU || p.seg1 < p.n_tiles) prefetch_tmap(&tb1);
+      if (EPI == EPI_STORE && p.seg2 < p.n_tiles) prefetch_tmap(&tb2);
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      auto full_bar = [&](int stage) { return smem_u32(&full[stage]) & kPeerBitMask; };
+      auto load_b = [&](int stage, int nt, int kb) {
+        uint8_t* sb = ring + stage * S::STAGE + S::A_BYTES;
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_load_2d_pair(sb, rank == 0 ? &tb0 : &tb1, full_bar(stage), kb * BK, nt * (BN / 2), pol_w);
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_load_2d_pair(sb, tb, full_bar(stage), kb * BK, row0 + rank * (BN / 2), pol_w);
+        }
+      };
+      int pre = 0;
+      if (pair < total_tiles) {
+        int mt0, nt0;
+        tile_coords(pair, p, mt0, nt0);
+        pre = min(STAGES, p.num_kb);
+        for (int kb = 0; kb < pre; ++kb) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * S::STAGE);
+          load_b(kb, nt0, kb);
+        }
+      }
+      pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
+        int mt, nt;
+        tile_coords(t, p, mt, nt);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!(t == pair && kb < pre)) {
+            if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE);
+            load_b(stage, nt, kb);
+          }
+          tma_load_2d_pair(ring + stage * S::STAGE, &ta, full_bar(stage), kb * BK, mt * 256 + rank * 128, pol_a);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(Dt<DT>::umma_fmt, 256, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = pair; t < total_tiles && ok; t += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(ring + stage * S::STAGE);
+          const uint32_t b0 = a0 + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_ss_pair(d, make_sw128_desc(a0 + kk * 32, 0, 1024), make_sw128_desc(b0 + kk * 32, 0, 1024),
+                             idesc, (kb | kk) != 0);
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) umma_commit_pair(&tfull[acc], 0x3);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = rank * 128 + quarter * 32 + lane;
+    const uint32_t tempty_leader = smem_u32(&tempty[0]) & kPeerBitMask;
+    int i = 0;
+    for (int t = pair; t < total_tiles; t += npairs, ++i) {
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      const int acc = i & 1;
+      const uint32_t acc_phase = (i >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      const int row = mt * 256 + row_in_tile;
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_remote(tempty_leader + acc * 8);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // every MMA, every epilogue and every remote arrival of the pair is done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // Split-K variant for few output tiles (weight streaming at M <= a few hundred).
 //
 // A cluster of `split` CTAs shares one output tile; CTA r of the cluster runs
@@ -575,6 +770,41 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1
   return launch_kernel(kern, dim3(grid), dim3(THREADS), S::TOTAL, st, 1, "gemm_kernel", ta, tb0, tb1, tb2, p);
 }
 
+template <int DT, int BN, int EPI, int STAGES>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& tb2,
+                const Params& p, cudaStream_t st) {
+  using S = PairSmem<BN, STAGES>;
+  auto kern = gemm_pair_kernel<DT, BN, EPI, STAGES>;
+  static int max_pairs[64] = {};
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  if (!max_pairs[dev.device]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL),
+                            "cudaFuncSetAttribute(gemm_pair)"))
+      return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (int rc = check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "cudaOccupancyMaxActiveClusters")) return rc;
+    max_pairs[dev.device] = std::max(1, n);
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int pairs = std::max(1, std::min(tiles, max_pairs[dev.device]));
+  return launch_kernel(kern, dim3(2 * pairs), dim3(THREADS), S::TOTAL, st, 2, "gemm_pair_kernel", ta, tb0, tb1, tb2, p);
+}
+
+// Pair (2-SM) tiles pay off once there are enough 256-row tiles to keep every SM pair busy.
+static bool use_pair(int64_t m, int64_t n_tiles, int sms) { return m >= 512 && ((m + 255) / 256) * n_tiles >= sms / 2; }
+
 template <int DT, int BN, int EPI>
 int launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& tb2,
                   const Params& p, int split, int stages, cudaStream_t st) {
@@ -744,6 +974,28 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
     if (int rc = tensor_map_2d(&tb1, w1, DT, n1, k, k, bn, BK)) return rc;
   if (n2)
     if (int rc = tensor_map_2d(&tb2, w2, DT, n2, k, k, bn, BK)) return rc;
+  // 2-SM pair tiles (256 rows) for large M: BN 256 when the weight blocks allow it, else 128
+  {
+    const int pbn = (constraint % 256 == 0 && n >= 1024) ? 256 : (constraint % 128 == 0 ? 128 : 0);
+    if (pbn && plan.split <= 1 && use_pair(m, (n + pbn - 1) / pbn, dev.sm_count)) {
+      Params q = p;
+      q.m_tiles = static_cast<int>((m + 255) / 256);
+      q.n_tiles = static_cast<int>((n + pbn - 1) / pbn);
+      q.seg1 = n1 || n2 ? static_cast<int>(n0 / pbn) : q.n_tiles;
+      q.seg2 = n2 ? static_cast<int>((n0 + n1) / pbn) : q.n_tiles;
+      CUtensorMap pa, pb0, pb1, pb2;
+      if (int rc = tensor_map_2d(&pa, x, DT, m, k, lda, 128, BK)) return rc;
+      if (int rc = tensor_map_2d(&pb0, w0, DT, n0, k, k, pbn / 2, BK)) return rc;
+      pb1 = pb0;
+      pb2 = pb0;
+      if (n1)
+        if (int rc = tensor_map_2d(&pb1, w1, DT, n1, k, k, pbn / 2, BK)) return rc;
+      if (n2)
+        if (int rc = tensor_map_2d(&pb2, w2, DT, n2, k, k, pbn / 2, BK)) return rc;
+      if (pbn == 256) return launch_pair<DT, 256, EPI_STORE, 6>(pa, pb0, pb1, pb2, q, st);
+      return launch_pair<DT, 128, EPI_STORE, 8>(pa, pb0, pb1, pb2, q, st);
+    }
+  }
   if (plan.split > 1) {
     switch (bn) {
       case 256: return launch_splitk<DT, 256, EPI_STORE>(ta, tb0, tb1, tb2, p, plan.split, plan.stages, st);
@@ -777,6 +1029,25 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
     plan = plan_small_m<DT, EPI_SWIGLU>(m_tiles, f, static_cast<int>((hidden + BK - 1) / BK), dev.sm_count, 1,
                                         dev.smem_optin);
     if (plan.bn) half = plan.bn / 2;
+  }
+  if (use_pair(m, (f + 127) / 128, dev.sm_count)) {
+    // pair tiles: rank 0 loads 128 gate rows, rank 1 the same 128 up rows
+    Params q{};
+    q.m = static_cast<int>(m);
+    q.n = static_cast<int>(f);
+    q.k = static_cast<int>(hidden);
+    q.num_kb = static_cast<int>((hidden + BK - 1) / BK);
+    q.m_tiles = static_cast<int>((m + 255) / 256);
+    q.n_tiles = static_cast<int>((f + 127) / 128);
+    q.seg1 = q.seg2 = q.n_tiles;
+    q.y = h;
+    q.ldy = f;
+    q.residual = nullptr;
+    CUtensorMap pa, pg, pu;
+    if (int rc = tensor_map_2d(&pa, x, DT, m, hidden, lda, 128, BK)) return rc;
+    if (int rc = tensor_map_2d(&pg, wg, DT, f, hidden, hidden, 128, BK)) return rc;
+    if (int rc = tensor_map_2d(&pu, wu, DT, f, hidden, hidden, 128, BK)) return rc;
+    return launch_pair<DT, 256, EPI_SWIGLU, 6>(pa, pg, pu, pu, q, st);
   }
   Params p{};
   p.m = static_cast<int>(m);
