@@ -50,8 +50,10 @@ def _args():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["forward", "gate_up_swiglu", "down_proj", "qkv_proj", "o_proj",
-                                       "rope_attention", "rmsnorm"],
-                    help="profiling helper: time only the graph replay or one kernel kind (268M shapes)")
+                                       "rope_attention", "rmsnorm", "qwen_forward"],
+                    help="profiling helper: time only the graph replay or one kernel kind (268M shapes), or "
+                         "the Qwen-shaped batched forward (--qwen-batch sequences of 512)")
+    ap.add_argument("--qwen-batch", type=int, default=64)
     return ap.parse_args()
 
 
@@ -78,9 +80,19 @@ def _blas_threads() -> int:
     return os.cpu_count() or 1
 
 
+def _use_all_host_threads():
+    """BLAS may inherit OMP_NUM_THREADS=1 from torchrun; the CPU baseline uses every core."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+    except Exception:
+        pass
+
+
 def _oracle_setup(cfg, seed=0):
     import numpy as np
     import oracle
+    _use_all_host_threads()
     from tinker_b200.eager_model import build_model
     m = build_model(cfg, seed=seed)
     w = {k: v.detach().float().numpy() for k, v in m.state_dict().items()}
@@ -353,6 +365,20 @@ def run_only(args):
     from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.only == "qwen_forward":
+        from tinker_b200.eager_model import QWEN25_05B_SHAPED
+        qcfg = QWEN25_05B_SHAPED
+        qtok = make_tokens(qcfg, args.qwen_batch, 512, seed=7)
+        qm = tinker_b200.optimize(build_model(qcfg, seed=0).to(dev), dtype=torch.bfloat16, cuda_graph=True,
+                                  graph_input_shape=tuple(qtok.shape), graph_vocab_size=qcfg.vocab_size,
+                                  graph_clone_output=False)
+        qm._static_input.copy_(qtok.to(dev))
+        for _ in range(args.warmup):
+            qm._graph.replay()
+        ms, _ = _time_replays(qm._graph, args.steps)
+        print(json.dumps({"only": args.only, "batch": args.qwen_batch, "steps": args.steps, "ms_mean": round(ms, 4),
+                          "tokens_per_s": round(args.qwen_batch * 512 / (ms * 1e-3))}), flush=True)
+        return
     cfg = LLAMA_268M
     tokens = make_tokens(cfg, 1, 128, seed=1)
     graph = args.only == "forward"
