@@ -102,6 +102,17 @@ TK_API int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k,
                       int num_kv_heads, int head_dim, int start_pos, int dtype, void* stream);
 
 /*
+ * The same causal GQA attention on q and k that already carry RoPE (the q|k|v
+ * projection applied it in its epilogue, tk_linear_rope): the kernel of
+ * tk_rope_attention without the rotation. Together with tk_linear_rope it
+ * replaces the q/k/v projections plus fused_attention in TinKerAttention.forward
+ * (tinker/modules/attention.py:55-70, tinker/kernels/fused_attention.py:195-231).
+ */
+TK_API int tk_causal_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                        const void* v, int64_t v_tok_stride, void* out, int64_t out_tok_stride, int batch,
+                        int seq, int num_heads, int num_kv_heads, int head_dim, int dtype, void* stream);
+
+/*
  * y[m, n] = x[m, k] . w[n, k]^T on tcgen05 (nn.Linear without bias), fp32
  * accumulation in TMEM. Replaces the nn.Linear projections the reference's
  * modules run through cuBLAS (tinker/modules/attention.py:53-55,64;
@@ -115,6 +126,21 @@ TK_API int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k,
 TK_API int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
               const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
               int64_t k, int dtype, void* stream);
+
+/*
+ * The fused q|k|v projection with RoPE in its epilogue: y = x . cat(wq, wk, wv)^T
+ * where the q and k columns of every row are rounded to dtype and then rotated
+ * (interleaved pairs, fp32 math) at position start_pos + (row mod seq), i.e. the
+ * rows are [batch, seq] tokens. cos_table / sin_table: float32 [table_rows,
+ * head_dim/2]. Replaces q_proj/k_proj/v_proj plus the RoPE kernel launches of
+ * TinKerAttention.forward (tinker/modules/attention.py:55-70,
+ * tinker/kernels/fused_attention.py:203-214, :19-69); the result feeds
+ * tk_causal_attention.
+ */
+TK_API int tk_linear_rope(const void* x, int64_t x_row_stride, const void* wq, int64_t nq, const void* wk, int64_t nk,
+                   const void* wv, int64_t nv, void* y, int64_t y_row_stride, int64_t m, int64_t k, int seq,
+                   int start_pos, int head_dim, const void* cos_table, const void* sin_table, int64_t table_rows,
+                   int dtype, void* stream);
 
 /*
  * h[m, f] = silu(x . w_gate^T) * (x . w_up^T): the gate and up projections as

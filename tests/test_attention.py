@@ -167,3 +167,103 @@ def test_from_module():
     assert (mod.num_heads, mod.num_kv_heads, mod.head_dim) == (8, 2, 64)
     for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
         torch.testing.assert_close(getattr(mod, n).weight.data, getattr(src, n).weight.data)
+
+
+def _qkv_rope_case(B, S, hidden, hq, hkv, d, dtype, start_pos, seed):
+    """x, q|k|v weights and RoPE tables for the projection-with-RoPE path."""
+    from tinker_b200.kernels.fused_attention import precompute_rope_tables
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(B, S, hidden, device="cuda", generator=g).to(dtype)
+    ws = [(torch.randn(n * d, hidden, device="cuda", generator=g) * hidden ** -0.5).to(dtype)
+          for n in (hq, hkv, hkv)]
+    cos, sin = precompute_rope_tables(d, S + start_pos + 5, 1e4, device="cuda")
+    return x, ws, cos, sin
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B, S, hidden, hq, hkv, d, start_pos",
+                         [(1, 128, 1024, 16, 4, 64, 0), (2, 200, 512, 8, 2, 64, 3), (3, 77, 896, 14, 2, 64, 0),
+                          (2, 160, 1024, 8, 2, 128, 11), (8, 512, 896, 14, 2, 64, 0)])
+def test_linear_rope_columns(dt, B, S, hidden, hq, hkv, d, start_pos):
+    """q|k|v projection with RoPE in the epilogue = linear, rounding, then the reference's RoPE
+    (tinker/kernels/fused_attention.py:53-69, :203-214) on the q and k heads; v unrotated."""
+    require_b200()
+    from tinker_b200.kernels.gemm import linear_rope
+    dtype = DTYPES[dt]
+    x, ws, cos, sin = _qkv_rope_case(B, S, hidden, hq, hkv, d, dtype, start_pos, seed=S + d)
+    y = linear_rope(x, *ws, cos, sin, d, start_pos)
+    assert y.shape == (B, S, (hq + 2 * hkv) * d)
+    xn = np32(x).reshape(B * S, hidden)
+    parts = [oracle.linear(xn, np32(w), out_dtype=NP_NAME[dtype]).reshape(B, S, -1) for w in ws]
+    ref = []
+    for i, (part, heads) in enumerate(zip(parts, (hq, hkv, hkv))):
+        if i < 2:
+            bhsd = part.reshape(B, S, heads, d).transpose(0, 2, 1, 3)
+            part = oracle.apply_rope(bhsd, np32(cos), np32(sin), start_pos, out_dtype=NP_NAME[dtype])
+            part = part.transpose(0, 2, 1, 3).reshape(B, S, heads * d)
+        ref.append(part)
+    ref = np.concatenate(ref, axis=-1)
+    tol = {torch.float16: 2e-3, torch.bfloat16: 8e-3}[dtype]
+    assert rel_err(np32(y), ref) <= tol
+    # the v columns carry no rotation
+    assert rel_err(np32(y[..., (hq + hkv) * d:]), parts[2]) <= tol
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B, S, hq, hkv, d, start_pos",
+                         [(1, 128, 16, 4, 64, 0), (2, 300, 8, 2, 64, 5), (4, 512, 14, 2, 64, 0),
+                          (2, 256, 8, 8, 128, 0), (1, 1, 4, 1, 64, 9), (2, 1000, 16, 4, 128, 0)])
+def test_rotated_projection_then_causal_attention(dt, B, S, hq, hkv, d, start_pos):
+    """linear_rope + causal_attention (the module path) = q|k|v projection + fused_attention of
+    the oracle, on the same inputs."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import causal_attention
+    from tinker_b200.kernels.gemm import linear_rope
+    dtype = DTYPES[dt]
+    hidden = 512
+    x, ws, cos, sin = _qkv_rope_case(B, S, hidden, hq, hkv, d, dtype, start_pos, seed=7 * S + hq)
+    qkv = linear_rope(x, *ws, cos, sin, d, start_pos)
+    hqd, hkvd = hq * d, hkv * d
+    out = causal_attention(qkv[..., :hqd], qkv[..., hqd:hqd + hkvd], qkv[..., hqd + hkvd:], hq, hkv, d)
+    xn = np32(x).reshape(B * S, hidden)
+    q, k, v = (oracle.linear(xn, np32(w), out_dtype=NP_NAME[dtype]).reshape(B, S, -1) for w in ws)
+    ref = oracle.attention(q, k, v, np32(cos), np32(sin), hq, hkv, d, start_pos, io_dtype=NP_NAME[dtype])
+    assert out.shape == (B, S, hqd)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+def test_causal_attention_equals_rope_attention_on_rotated_inputs():
+    """The no-RoPE kernel on q, k rotated by the RoPE kernel's own arithmetic gives the same
+    result as the RoPE kernel on the raw inputs (one kernel, two entry points)."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import causal_attention, fused_attention, precompute_rope_tables
+    B, S, hq, hkv, d = 2, 384, 8, 2, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, S, hq * d, device="cuda", generator=g).to(torch.float16)
+    k = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(torch.float16)
+    v = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(torch.float16)
+    cos, sin = precompute_rope_tables(d, S, device="cuda")
+
+    def rot(t, heads):
+        x = t.float().view(B, S, heads, d // 2, 2)
+        c, s = cos[:S].view(1, S, 1, d // 2), sin[:S].view(1, S, 1, d // 2)
+        e, o = x[..., 0], x[..., 1]
+        return torch.stack([e * c - o * s, e * s + o * c], -1).reshape(B, S, heads * d).to(t.dtype)
+
+    a = fused_attention(q, k, v, cos, sin, hq, hkv, d)
+    b = causal_attention(rot(q, hq), rot(k, hkv), v, hq, hkv, d)
+    torch.testing.assert_close(a, b, atol=2e-3, rtol=2e-3)
+
+
+def test_linear_rope_rejects_bad_arguments():
+    require_b200()
+    from tinker_b200 import _lib
+    from tinker_b200.kernels.gemm import linear_rope
+    from tinker_b200.kernels.fused_attention import precompute_rope_tables
+    x = torch.randn(1, 8, 256, device="cuda", dtype=torch.float16)
+    w = torch.randn(128, 256, device="cuda", dtype=torch.float16)
+    cos, sin = precompute_rope_tables(64, 8, device="cuda")
+    with pytest.raises(_lib.TinkerKernelError, match="table"):
+        linear_rope(x, w, w, w, cos, sin, 64, start_pos=1)
+    with pytest.raises(TypeError, match="float32"):
+        linear_rope(x, w, w, w, cos.half(), sin.half(), 64)

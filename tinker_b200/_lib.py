@@ -33,7 +33,10 @@ SIGNATURES = {
     "tk_add_rmsnorm": [_P, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _P],
     "tk_swiglu": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P],
     "tk_rope_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _I, _P],
+    "tk_causal_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _P],
     "tk_linear": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _P],
+    "tk_linear_rope": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I,
+                       _P],
     "tk_gate_up_swiglu": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_swiglu_ffn": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_swiglu_ffn_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],

@@ -1,22 +1,28 @@
 // Fused RoPE + GQA/MQA/MHA causal attention on tcgen05 tensor cores.
 //
-// One CTA (4 warps, thread i owns query row i of the tile) computes a 128-row
-// query tile of one (batch, query head):
-//   * TMA loads the raw Q tile once and, per 128-key tile, the raw K and V tiles
-//     of KV head h / groups straight from the [batch, seq, heads, head_dim]
-//     projection layout (token strides are free, so q/k/v may be column slices of
-//     one fused QKV output) into 128-byte-swizzled shared memory.
-//   * RoPE is applied on load: each thread rotates the interleaved pairs of its
-//     Q row (once) and its K row (every tile) in place in shared memory, in fp32,
-//     rounding back to the input dtype as the reference does before its
-//     attention kernel (tinker/kernels/fused_attention.py:203-214, :53-69).
-//   * S = Q K^T runs as tcgen05.mma (M=128, N=128, K=head_dim) into TMEM; the
-//     online softmax reads S with tcgen05.ld, writes P (rounded to the input
-//     dtype) to shared memory and rescales the running O in TMEM; O += P V is a
-//     second tcgen05.mma with V as an MN-major operand.
-//   * Causal tiles above the diagonal are skipped; only the diagonal tile is masked.
-// The arithmetic follows _attention_kernel (tinker/kernels/fused_attention.py:74-154):
-// scale 1/sqrt(head_dim), running max / sum in fp32, output divided by the sum.
+// One CTA computes a 128-row query tile of one (batch, query head) with four
+// warp roles working through mbarriers:
+//   * warp 4 (TMA): loads the raw Q tile once and streams the raw K and V tiles
+//     of KV head h / groups through a two-stage ring straight from the
+//     [batch, seq, heads, head_dim] projection layout (token strides are free, so
+//     q/k/v may be column slices of one fused QKV output) into 128-byte-swizzled
+//     shared memory.
+//   * warps 6-7 (RoPE): rotate the interleaved pairs of every K row in place in
+//     shared memory, in fp32, rounding back to the input dtype as the reference
+//     does before its attention kernel (tinker/kernels/fused_attention.py:203-214,
+//     :53-69). Warps 0-3 rotate the Q tile the same way, once.
+//   * warp 5 (MMA): S_j = Q K_j^T as tcgen05.mma (M=128, N=128, K=head_dim) into
+//     one of two TMEM S buffers, so S_{j+1} is computed while S_j is in softmax;
+//     then O += P_j V_j with V as an MN-major operand into the TMEM O accumulator.
+//   * warps 0-3 (softmax, thread i owns query row i): read S_j with tcgen05.ld,
+//     mask the diagonal tile, run the online softmax with exp2, write P_j (rounded
+//     to the input dtype) to shared memory and rescale the running O in TMEM.
+//     The running maximum is only moved when a tile raises it by more than
+//     2^8 (a lazy rescale): P stays below 256 and O is rescaled on few tiles.
+//     The final O / l is written by the same threads.
+// Causal tiles above the diagonal are skipped. The arithmetic follows
+// _attention_kernel (tinker/kernels/fused_attention.py:74-154): scale
+// 1/sqrt(head_dim), running max / sum in fp32, output divided by the sum.
 #include <cmath>
 
 #include "tk_common.cuh"
@@ -27,7 +33,9 @@ namespace attn {
 
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int THREADS = 128;
+constexpr int THREADS = 320;  // warps 0-3 softmax, 4 TMA, 5 MMA, 6-9 RoPE of K (one row per thread)
+constexpr int ROPE_K_THREADS = 128;
+constexpr float LAZY_RESCALE_LOG2 = 8.0f;  // move the running max only when it grows by more than 2^8
 
 template <int D>
 struct Smem {
@@ -36,12 +44,27 @@ struct Smem {
   static constexpr int V_BYTES = BKV * D * 2;
   static constexpr int P_BYTES = BQ * BKV * 2;
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + Q_BYTES;
-  static constexpr int V_OFF = K_OFF + K_BYTES;
-  static constexpr int P_OFF = V_OFF + V_BYTES;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;      // two stages
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;  // two stages
+  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;
   static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  static constexpr int TOTAL = 1024 + BAR_OFF + 4 * 8 + 16;
-  static constexpr uint32_t TMEM_COLS = 256;  // S: 128 columns, O: head_dim columns
+  static constexpr int NUM_BARS = 16;
+  static constexpr int TOTAL = 1024 + BAR_OFF + NUM_BARS * 8 + 16;
+  static constexpr uint32_t TMEM_COLS = 512;  // S0: 0-127, S1: 128-255, O: 256..256+head_dim
+};
+
+// mbarrier slots
+enum : int {
+  B_Q_FULL = 0,    // Q tile landed (TMA transaction bytes)
+  B_Q_READY = 1,   // Q rotated (128 softmax threads)
+  B_K_FULL = 2,    // [2] K stage landed
+  B_V_FULL = 4,    // [2] V stage landed
+  B_K_READY = 6,   // [2] K stage rotated (128 RoPE threads)
+  B_KV_EMPTY = 8,  // [2] S and P.V of the stage finished (UMMA commit)
+  B_S_FULL = 10,   // [2] S buffer written (UMMA commit)
+  B_S_FREE = 12,   // [2] S buffer read into registers (128 softmax threads)
+  B_P_FULL = 14,   // P written and O rescaled (128 softmax threads)
+  B_PV_DONE = 15,  // P.V finished (UMMA commit)
 };
 
 struct Params {
@@ -56,7 +79,7 @@ struct Params {
 };
 
 // Load 4 consecutive table entries (pair indices i0..i0+3) of row `pos` as fp32.
-__device__ __forceinline__ void load_cs4(const void* t, int dt, int64_t off, float (&v)[4]) {
+__device__ __forceinline__ void load_cs4(const void* t, int dt, int64_t off, float* v) {
   if (dt == TK_F32) {
     const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(t) + off);
     v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
@@ -74,34 +97,50 @@ __device__ __forceinline__ void load_cs4(const void* t, int dt, int64_t off, flo
   }
 }
 
-// Rotate row `r` of a swizzled [128 x D] tile in place by the RoPE angle of position `pos`.
-template <int DT, int D>
-__device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int64_t pos, const Params& p) {
+// RoPE of one row of a swizzled [128 x D] tile, in 64-column blocks: the 32 cos and
+// 32 sin values of a block are loaded first (all in flight at once), then the
+// block's 8 chunks of the row are rotated in place in fp32 and rounded back.
+__device__ __forceinline__ void rope_load_block(const Params& p, int64_t pos, int blk, int half_d, float (&c)[32],
+                                                float (&s)[32]) {
+  const int64_t off = pos * half_d + blk * 32;
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    load_cs4(p.cos_t, p.table_dtype, off + ch * 4, c + ch * 4);
+    load_cs4(p.sin_t, p.table_dtype, off + ch * 4, s + ch * 4);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void rope_apply_block(uint8_t* tile, int r, int blk, const float (&c)[32],
+                                                 const float (&s)[32]) {
   using Dx = Dt<DT>;
-  const int64_t trow = pos * (D / 2);
 #pragma unroll
-  for (int blk = 0; blk < D / 64; ++blk) {
+  for (int ch = 0; ch < 8; ++ch) {
+    uint4* addr = reinterpret_cast<uint4*>(tile + blk * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16));
+    uint4 u = *addr;
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      uint4* addr = reinterpret_cast<uint4*>(tile + blk * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16));
-      uint4 u = *addr;
-      uint32_t w[4] = {u.x, u.y, u.z, u.w};
-      const int i0 = blk * 32 + ch * 4;  // first pair index of this 16-byte chunk
-      float c[4], s[4];
-      load_cs4(p.cos_t, p.table_dtype, trow + i0, c);
-      load_cs4(p.sin_t, p.table_dtype, trow + i0, s);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 x = Dx::unpack(*reinterpret_cast<typename Dx::T2*>(&w[i]));
-        typename Dx::T2 o = Dx::pack(x.x * c[i] - x.y * s[i], x.x * s[i] + x.y * c[i]);
-        w[i] = *reinterpret_cast<uint32_t*>(&o);
-      }
-      *addr = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = Dx::unpack(*reinterpret_cast<typename Dx::T2*>(&w[i]));
+      const float cc = c[ch * 4 + i], ss = s[ch * 4 + i];
+      typename Dx::T2 o = Dx::pack(x.x * cc - x.y * ss, x.x * ss + x.y * cc);
+      w[i] = *reinterpret_cast<uint32_t*>(&o);
     }
+    *addr = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
 template <int DT, int D>
+__device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int64_t pos, const Params& p) {
+#pragma unroll
+  for (int blk = 0; blk < D / 64; ++blk) {
+    float c[32], s[32];
+    rope_load_block(p, pos, blk, D / 2, c, s);
+    rope_apply_block<DT>(tile, r, blk, c, s);
+  }
+}
+
+template <int DT, int D, bool ROPE>
 __global__ void __launch_bounds__(THREADS, 1)
     rope_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const Params p) {
@@ -114,13 +153,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sv = smem + S::V_OFF;
   uint8_t* sp = smem + S::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* s_done = bars + 1;
-  uint64_t* pv_done = bars + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NUM_BARS);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
   const int h = blockIdx.y;
   const int b = blockIdx.z;
@@ -129,12 +166,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_kv = qt + 1;  // causal: key tiles 0..qt
 
   if (tid == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(s_done, 1);
-    mbar_init(pv_done, 1);
+    mbar_init(bars + B_Q_FULL, 1);
+    mbar_init(bars + B_Q_READY, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bars + B_K_FULL + i, 1);
+      mbar_init(bars + B_V_FULL + i, 1);
+      mbar_init(bars + B_K_READY + i, ROPE_K_THREADS);
+      mbar_init(bars + B_KV_EMPTY + i, 1);
+      mbar_init(bars + B_S_FULL + i, 1);
+      mbar_init(bars + B_S_FREE + i, 128);
+    }
+    mbar_init(bars + B_P_FULL, 128);
+    mbar_init(bars + B_PV_DONE, 1);
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 5) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
@@ -142,174 +188,215 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t t_s = tmem_base;
-  const uint32_t t_o = tmem_base + 128;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  {
-    // the RoPE table rows this thread rotates with (Q row, first K row) do not depend
-    // on the previous kernel: start pulling them into L1 while it finishes
-    const int es = p.table_dtype == TK_F32 ? 4 : 2;
-    const int row_bytes = (D / 2) * es;
-    const int64_t qpos = static_cast<int64_t>(p.start_pos) + q0 + tid;
-    const int64_t kpos = static_cast<int64_t>(p.start_pos) + tid;
-    if (q0 + tid < p.seq && qpos < p.table_rows)
-      for (int b = 0; b < row_bytes; b += 128) {
-        prefetch_l1(static_cast<const char*>(p.cos_t) + qpos * row_bytes + b);
-        prefetch_l1(static_cast<const char*>(p.sin_t) + qpos * row_bytes + b);
-      }
-    if (tid < p.seq && kpos < p.table_rows)
-      for (int b = 0; b < row_bytes; b += 128) {
-        prefetch_l1(static_cast<const char*>(p.cos_t) + kpos * row_bytes + b);
-        prefetch_l1(static_cast<const char*>(p.sin_t) + kpos * row_bytes + b);
-      }
-  }
+  const uint32_t t_o = tmem_base + 256;
 
-  if (tid == 0) {
-    pdl_launch_dependents();
-    prefetch_tmap(&tq);
-    prefetch_tmap(&tk);
-    prefetch_tmap(&tv);
-    pdl_wait();  // q, k, v are written by the previous kernel
-    mbar_arrive_expect_tx(kv_full, S::Q_BYTES + S::K_BYTES + S::V_BYTES);
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      pdl_launch_dependents();
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      pdl_wait();  // q, k, v are written by the previous kernel
+      mbar_arrive_expect_tx(bars + B_Q_FULL, S::Q_BYTES);
 #pragma unroll
-    for (int blk = 0; blk < D / 64; ++blk) {
-      tma_load_3d(sq + blk * 128 * 128, &tq, kv_full, h * D + blk * 64, q0, b);
-      tma_load_3d(sk + blk * 128 * 128, &tk, kv_full, kvh * D + blk * 64, 0, b);
-      tma_load_3d(sv + blk * 128 * 128, &tv, kv_full, kvh * D + blk * 64, 0, b);
+      for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(sq + blk * 128 * 128, &tq, bars + B_Q_FULL, h * D + blk * 64, q0, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(bars + B_KV_EMPTY + st, ((j >> 1) - 1) & 1)) break;
+        uint8_t* k_dst = sk + st * S::K_BYTES;
+        uint8_t* v_dst = sv + st * S::V_BYTES;
+        mbar_arrive_expect_tx(bars + B_K_FULL + st, S::K_BYTES);
+#pragma unroll
+        for (int blk = 0; blk < D / 64; ++blk)
+          tma_load_3d(k_dst + blk * 128 * 128, &tk, bars + B_K_FULL + st, kvh * D + blk * 64, j * BKV, b);
+        mbar_arrive_expect_tx(bars + B_V_FULL + st, S::V_BYTES);
+#pragma unroll
+        for (int blk = 0; blk < D / 64; ++blk)
+          tma_load_3d(v_dst + blk * 128 * 128, &tv, bars + B_V_FULL + st, kvh * D + blk * 64, j * BKV, b);
+      }
     }
-  }
+  } else if (warp == 5) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(Dx::umma_fmt, BQ, BKV, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc_f16(Dx::umma_fmt, BQ, D, 0, 1);
+      // without RoPE the MMA reads the Q and K tiles as TMA lands them
+      bool ok = mbar_wait(bars + (ROPE ? B_Q_READY : B_Q_FULL), 0);
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          const int st = j & 1;
+          if (!mbar_wait(bars + (ROPE ? B_K_READY : B_K_FULL) + st, (j >> 1) & 1)) break;
+          if (j >= 2 && !mbar_wait(bars + B_S_FREE + st, ((j >> 1) - 1) & 1)) break;
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(sk + st * S::K_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+            umma_f16_ss(tmem_base + st * 128, make_sw128_desc(smem_u32(sq) + off, 0, 1024),
+                        make_sw128_desc(k_base + off, 0, 1024), idesc_s, kk != 0);
+          }
+          umma_commit(bars + B_S_FULL + st);
+        }
+        if (j >= 1) {
+          const int i = j - 1;
+          const int si = i & 1;
+          if (!mbar_wait(bars + B_P_FULL, i & 1)) break;
+          if (!mbar_wait(bars + B_V_FULL + si, (i >> 1) & 1)) break;
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(sv + si * S::V_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+            umma_f16_ss(t_o, make_sw128_desc(smem_u32(sp) + aoff, 0, 1024),
+                        make_sw128_desc(v_base + kk * 16 * 128, BKV * 128, 1024), idesc_o,
+                        (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bars + B_PV_DONE);
+          umma_commit(bars + B_KV_EMPTY + si);
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- RoPE of the K stages (thread = key row) ----------------
+    if constexpr (ROPE) {
+      const int t = tid - 6 * 32;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const int k_row = j * BKV + t;  // rows past the sequence are zero-filled by TMA and left alone
+        const bool valid = k_row < p.seq;
+        const int64_t kpos = static_cast<int64_t>(p.start_pos) + k_row;
+        float c[32], sn[32];
+        if (valid) rope_load_block(p, kpos, 0, D / 2, c, sn);  // in flight while the K tile lands
+        if (!mbar_wait(bars + B_K_FULL + st, (j >> 1) & 1)) break;
+        uint8_t* ks_ = sk + st * S::K_BYTES;
+        if (valid) {
+          rope_apply_block<DT>(ks_, t, 0, c, sn);
+#pragma unroll
+          for (int blk = 1; blk < D / 64; ++blk) {
+            rope_load_block(p, kpos, blk, D / 2, c, sn);
+            rope_apply_block<DT>(ks_, t, blk, c, sn);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bars + B_K_READY + st);
+      }
+    }
+  } else {
+    // ---------------- softmax / correction / output (thread = query row) ----------------
+    const int q_row = q0 + tid;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    bool ok = true;
+    if constexpr (ROPE) {
+      const int64_t qpos = static_cast<int64_t>(p.start_pos) + q_row;
+      const bool valid = q_row < p.seq;
+      float c[32], sn[32];
+      if (valid) rope_load_block(p, qpos, 0, D / 2, c, sn);  // in flight while the Q tile lands
+      ok = mbar_wait(bars + B_Q_FULL, 0);
+      if (ok && valid) {
+        rope_apply_block<DT>(sq, tid, 0, c, sn);
+#pragma unroll
+        for (int blk = 1; blk < D / 64; ++blk) {
+          rope_load_block(p, qpos, blk, D / 2, c, sn);
+          rope_apply_block<DT>(sq, tid, blk, c, sn);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bars + B_Q_READY);
+    }
 
-  constexpr uint32_t idesc_s = make_idesc_f16(Dx::umma_fmt, BQ, BKV, 0, 0);
-  constexpr uint32_t idesc_o = make_idesc_f16(Dx::umma_fmt, BQ, D, 0, 1);
-  const int q_row = q0 + tid;
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;
-
-  for (int j = 0; j < n_kv; ++j) {
-    if (!mbar_wait(kv_full, j & 1)) { ok = false; break; }
-    // RoPE on load (rows past the sequence are zero-filled by TMA and left alone)
-    if (j == 0 && q_row < p.seq) rope_row_inplace<DT, D>(sq, tid, static_cast<int64_t>(p.start_pos) + q_row, p);
-    const int k_row = j * BKV + tid;
-    if (k_row < p.seq) rope_row_inplace<DT, D>(sk, tid, static_cast<int64_t>(p.start_pos) + k_row, p);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    if (tid == 0) {
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0; ok && j < n_kv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(bars + B_S_FULL + sb, (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
+      float s[BKV];
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-        umma_f16_ss(t_s, make_sw128_desc(smem_u32(sq) + off, 0, 1024), make_sw128_desc(smem_u32(sk) + off, 0, 1024),
-                    idesc_s, kk != 0);
+      for (int c = 0; c < BKV; c += 32)
+        tmem_ld32(tmem_base + sb * 128 + lane_off + c, *reinterpret_cast<float(*)[32]>(&s[c]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bars + B_S_FREE + sb);
+
+      const bool diag = (j == qt);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        float v = s[c] * p.scale_log2;
+        if (diag && (j * BKV + c) > q_row) v = -INFINITY;
+        s[c] = v;
+        mx = fmaxf(mx, v);
       }
-      umma_commit(s_done);
-    }
-    if (!mbar_wait(s_done, j & 1)) { ok = false; break; }
-    tc_fence_after();
+      // lazy rescale: keep the old maximum unless this tile exceeds it by more than 2^8
+      float m_use = m_run, alpha = 1.f;
+      if (mx > m_run + LAZY_RESCALE_LOG2) {
+        m_use = mx;
+        alpha = exp2f(m_run - mx);
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        s[c] = exp2f(s[c] - m_use);
+        rs += s[c];
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_use;
 
-    // ---- online softmax on row tid ----
-    float s[BKV];
+      if (j > 0) {
+        // P and the O accumulator are still in use by the previous P.V
+        if (!mbar_wait(bars + B_PV_DONE, (j - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+      }
 #pragma unroll
-    for (int c = 0; c < BKV; c += 32) tmem_ld32(t_s + lane_off + c, *reinterpret_cast<float(*)[32]>(&s[c]));
-    tmem_wait_ld();
-    const bool diag = (j == qt);
-    float mx = -INFINITY;
+      for (int c = 0; c < BKV / 8; ++c) {
+        uint32_t w[4];
 #pragma unroll
-    for (int c = 0; c < BKV; ++c) {
-      float v = s[c] * p.scale_log2;
-      if (diag && (j * BKV + c) > q_row) v = -INFINITY;
-      s[c] = v;
-      mx = fmaxf(mx, v);
+        for (int i = 0; i < 4; ++i) {
+          typename Dx::T2 hv = Dx::pack(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        uint8_t* dst = sp + (c >> 3) * (128 * 128) + tid * 128 + (((c & 7) ^ (tid & 7)) * 16);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(t_o + lane_off + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_o + lane_off + c, o);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bars + B_P_FULL);
     }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = exp2f(m_run - m_new);
-    float rs = 0.f;
-#pragma unroll
-    for (int c = 0; c < BKV; ++c) {
-      s[c] = exp2f(s[c] - m_new);
-      rs += s[c];
-    }
-    l_run = l_run * alpha + rs;
-    m_run = m_new;
 
-    if (j > 0) {
-      // P and the O accumulator are still in use by the previous P.V
-      if (!mbar_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+    if (ok && mbar_wait(bars + B_PV_DONE, (n_kv - 1) & 1)) {
       tc_fence_after();
-    }
-#pragma unroll
-    for (int c = 0; c < BKV / 8; ++c) {
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        typename Dx::T2 hv = Dx::pack(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
-        w[i] = *reinterpret_cast<uint32_t*>(&hv);
-      }
-      uint8_t* dst = sp + (c >> 3) * (128 * 128) + tid * 128 + (((c & 7) ^ (tid & 7)) * 16);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      const float inv_l = 1.0f / l_run;
+      using T = typename Dx::T;
+      T* dst = reinterpret_cast<T*>(p.out) +
+               (static_cast<int64_t>(b) * p.seq + q_row) * p.out_tok_stride + static_cast<int64_t>(h) * D;
 #pragma unroll
       for (int c = 0; c < D; c += 32) {
         float o[32];
         tmem_ld32(t_o + lane_off + c, o);
         tmem_wait_ld();
+        if (q_row < p.seq) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-        tmem_st32(t_o + lane_off + c, o);
-      }
-      tmem_wait_st();
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    if (tid == 0) {
-      tc_fence_after();
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
 #pragma unroll
-      for (int kk = 0; kk < BKV / 16; ++kk) {
-        const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-        const uint64_t ad = make_sw128_desc(smem_u32(sp) + aoff, 0, 1024);
-        const uint64_t bd = make_sw128_desc(smem_u32(sv) + kk * 16 * 128, BKV * 128, 1024);
-        umma_f16_ss(t_o, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-      }
-      umma_commit(pv_done);
-      if (j + 1 < n_kv) {
-        // K and V of the next tile overwrite buffers the P.V just issued still reads
-        if (mbar_wait(pv_done, j & 1)) {
-          mbar_arrive_expect_tx(kv_full, S::K_BYTES + S::V_BYTES);
-#pragma unroll
-          for (int blk = 0; blk < D / 64; ++blk) {
-            tma_load_3d(sk + blk * 128 * 128, &tk, kv_full, kvh * D + blk * 64, (j + 1) * BKV, b);
-            tma_load_3d(sv + blk * 128 * 128, &tv, kv_full, kvh * D + blk * 64, (j + 1) * BKV, b);
+            for (int i = 0; i < 4; ++i) {
+              typename Dx::T2 hv = Dx::pack(o[q * 8 + 2 * i] * inv_l, o[q * 8 + 2 * i + 1] * inv_l);
+              w[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            reinterpret_cast<uint4*>(dst + c)[q] = make_uint4(w[0], w[1], w[2], w[3]);
           }
-        }
-      }
-    }
-  }
-
-  if (ok && mbar_wait(pv_done, (n_kv - 1) & 1)) {
-    tc_fence_after();
-    const float inv_l = 1.0f / l_run;
-    using T = typename Dx::T;
-    T* dst = reinterpret_cast<T*>(p.out) +
-             (static_cast<int64_t>(b) * p.seq + q_row) * p.out_tok_stride + static_cast<int64_t>(h) * D;
-#pragma unroll
-    for (int c = 0; c < D; c += 32) {
-      float o[32];
-      tmem_ld32(t_o + lane_off + c, o);
-      tmem_wait_ld();
-      if (q_row < p.seq) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            typename Dx::T2 hv = Dx::pack(o[q * 8 + 2 * i] * inv_l, o[q * 8 + 2 * i + 1] * inv_l);
-            w[i] = *reinterpret_cast<uint32_t*>(&hv);
-          }
-          reinterpret_cast<uint4*>(dst + c)[q] = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
@@ -317,13 +404,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
 }
 
-template <int DT, int D>
+template <int DT, int D, bool ROPE>
 int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, int64_t vs, Params p,
            cudaStream_t st) {
   using S = Smem<D>;
@@ -332,7 +419,7 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
   if (int rc = tensor_map_3d(&tq, q, DT, uint64_t(p.num_heads) * D, Sq, B, qs, qs * Sq, 64, BQ, 1)) return rc;
   if (int rc = tensor_map_3d(&tk_, k, DT, uint64_t(p.num_kv_heads) * D, Sq, B, ks, ks * Sq, 64, BKV, 1)) return rc;
   if (int rc = tensor_map_3d(&tv, v, DT, uint64_t(p.num_kv_heads) * D, Sq, B, vs, vs * Sq, 64, BKV, 1)) return rc;
-  auto kern = rope_attention_kernel<DT, D>;
+  auto kern = rope_attention_kernel<DT, D, ROPE>;
   static bool configured[64] = {};
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
@@ -343,7 +430,53 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
     configured[dev.device] = true;
   }
   return launch_kernel(kern, dim3(p.n_qtiles, p.num_heads, p.batch), dim3(THREADS), S::TOTAL, st, 1,
-                       "rope_attention_kernel", tq, tk_, tv, p);
+                       ROPE ? "rope_attention_kernel" : "causal_attention_kernel", tq, tk_, tv, p);
+}
+
+template <bool ROPE>
+int dispatch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, int64_t vs, const Params& p,
+             int dtype, int head_dim, cudaStream_t st) {
+  if (dtype == TK_F16) {
+    if (head_dim == 64) return launch<TK_F16, 64, ROPE>(q, qs, k, ks, v, vs, p, st);
+    return launch<TK_F16, 128, ROPE>(q, qs, k, ks, v, vs, p, st);
+  }
+  if (head_dim == 64) return launch<TK_BF16, 64, ROPE>(q, qs, k, ks, v, vs, p, st);
+  return launch<TK_BF16, 128, ROPE>(q, qs, k, ks, v, vs, p, st);
+}
+
+// Argument checks shared by both entry points; fills the kernel parameters.
+int prepare(const char* what, const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+            const void* v, int64_t v_tok_stride, void* out, int64_t out_tok_stride, int batch, int seq,
+            int num_heads, int num_kv_heads, int head_dim, int dtype, Params* p, bool* empty) {
+  *empty = false;
+  if (!half_dtype(dtype)) return fail_invalid("attention: dtype must be F16 or BF16");
+  if (head_dim != 64 && head_dim != 128) return set_error(TK_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0) return fail_invalid("attention: invalid sizes");
+  if (num_heads % num_kv_heads != 0) return fail_invalid("attention: num_heads must be a multiple of num_kv_heads");
+  if (q_tok_stride < int64_t(num_heads) * head_dim || k_tok_stride < int64_t(num_kv_heads) * head_dim ||
+      v_tok_stride < int64_t(num_kv_heads) * head_dim || out_tok_stride < int64_t(num_heads) * head_dim)
+    return fail_invalid("attention: token stride smaller than heads * head_dim");
+  if (q_tok_stride % 8 || k_tok_stride % 8 || v_tok_stride % 8 || out_tok_stride % 8)
+    return fail_invalid("attention: token strides must be multiples of 8 elements");
+  if (num_heads > 65535 || batch > 65535) return fail_invalid("attention: too many heads or batches");
+  if (batch == 0 || seq == 0) {  // empty tensors may carry NULL data pointers
+    *empty = true;
+    return TK_OK;
+  }
+  if (!q || !k || !v || !out) return fail_invalid("attention: NULL pointer");
+  if (!aligned16(out)) return fail_invalid("attention: out must be 16-byte aligned");
+  (void)what;
+  *p = Params{};
+  p->batch = batch;
+  p->seq = seq;
+  p->num_heads = num_heads;
+  p->num_kv_heads = num_kv_heads;
+  p->groups = num_heads / num_kv_heads;
+  p->n_qtiles = (seq + BQ - 1) / BQ;
+  p->out = out;
+  p->out_tok_stride = out_tok_stride;
+  p->scale_log2 = static_cast<float>((1.0 / std::sqrt(double(head_dim))) * 1.4426950408889634);
+  return TK_OK;
 }
 
 }  // namespace attn
@@ -355,44 +488,38 @@ extern "C" int tk_rope_attention(const void* q, int64_t q_tok_stride, const void
                                  int seq, int num_heads, int num_kv_heads, int head_dim, int start_pos, int dtype,
                                  void* stream) {
   using namespace tk;
-  if (!half_dtype(dtype)) return fail_invalid("rope_attention: dtype must be F16 or BF16");
   if (!valid_dtype(table_dtype)) return fail_invalid("rope_attention: table dtype must be F16, BF16 or F32");
-  if (head_dim != 64 && head_dim != 128) return set_error(TK_ERR_UNSUPPORTED, "rope_attention: head_dim must be 64 or 128");
-  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || start_pos < 0)
-    return fail_invalid("rope_attention: invalid sizes");
-  if (num_heads % num_kv_heads != 0) return fail_invalid("rope_attention: num_heads must be a multiple of num_kv_heads");
-  if (q_tok_stride < int64_t(num_heads) * head_dim || k_tok_stride < int64_t(num_kv_heads) * head_dim ||
-      v_tok_stride < int64_t(num_kv_heads) * head_dim || out_tok_stride < int64_t(num_heads) * head_dim)
-    return fail_invalid("rope_attention: token stride smaller than heads * head_dim");
-  if (q_tok_stride % 8 || k_tok_stride % 8 || v_tok_stride % 8 || out_tok_stride % 8)
-    return fail_invalid("rope_attention: token strides must be multiples of 8 elements");
+  if (start_pos < 0) return fail_invalid("rope_attention: invalid sizes");
+  attn::Params p{};
+  bool empty = false;
+  if (int rc = attn::prepare("rope_attention", q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, out,
+                             out_tok_stride, batch, seq, num_heads, num_kv_heads, head_dim, dtype, &p, &empty))
+    return rc;
   if (int64_t(start_pos) + seq > table_rows)
     return fail_invalid("rope_attention: start_pos + seq exceeds the RoPE table length");
-  if (num_heads > 65535 || batch > 65535) return fail_invalid("rope_attention: too many heads or batches");
-  if (batch == 0 || seq == 0) return TK_OK;  // empty tensors may carry NULL data pointers
-  if (!q || !k || !v || !cos_table || !sin_table || !out) return fail_invalid("rope_attention: NULL pointer");
-  if (!aligned16(out) || !aligned16(cos_table) || !aligned16(sin_table))
-    return fail_invalid("rope_attention: out and the RoPE tables must be 16-byte aligned");
-  attn::Params p{};
-  p.batch = batch;
-  p.seq = seq;
-  p.num_heads = num_heads;
-  p.num_kv_heads = num_kv_heads;
-  p.groups = num_heads / num_kv_heads;
+  if (empty) return TK_OK;
+  if (!cos_table || !sin_table) return fail_invalid("rope_attention: NULL pointer");
+  if (!aligned16(cos_table) || !aligned16(sin_table))
+    return fail_invalid("rope_attention: the RoPE tables must be 16-byte aligned");
   p.start_pos = start_pos;
-  p.n_qtiles = (seq + attn::BQ - 1) / attn::BQ;
   p.table_rows = table_rows;
   p.cos_t = cos_table;
   p.sin_t = sin_table;
   p.table_dtype = table_dtype;
-  p.out = out;
-  p.out_tok_stride = out_tok_stride;
-  p.scale_log2 = static_cast<float>((1.0 / std::sqrt(double(head_dim))) * 1.4426950408889634);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TK_F16) {
-    if (head_dim == 64) return attn::launch<TK_F16, 64>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, st);
-    return attn::launch<TK_F16, 128>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, st);
-  }
-  if (head_dim == 64) return attn::launch<TK_BF16, 64>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, st);
-  return attn::launch<TK_BF16, 128>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, st);
+  return attn::dispatch<true>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, dtype, head_dim,
+                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tk_causal_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                                   const void* v, int64_t v_tok_stride, void* out, int64_t out_tok_stride, int batch,
+                                   int seq, int num_heads, int num_kv_heads, int head_dim, int dtype, void* stream) {
+  using namespace tk;
+  attn::Params p{};
+  bool empty = false;
+  if (int rc = attn::prepare("causal_attention", q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, out,
+                             out_tok_stride, batch, seq, num_heads, num_kv_heads, head_dim, dtype, &p, &empty))
+    return rc;
+  if (empty) return TK_OK;
+  return attn::dispatch<false>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, dtype, head_dim,
+                               static_cast<cudaStream_t>(stream));
 }

@@ -45,6 +45,12 @@ struct Params {
   void* y;
   int64_t ldy;
   const void* residual;  // optional, [m, n] with row stride ldy
+  // RoPE epilogue (plain store only): columns [0, rope_cols) are the q and k heads of a
+  // fused q|k|v projection; row r sits at position rope_start + r % rope_seq.
+  int rope_cols;         // 0: no RoPE
+  int rope_seq, rope_start, rope_half_d;
+  const float* rope_cos;  // [table_rows, rope_half_d] float32
+  const float* rope_sin;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mt, int& nt) {
@@ -113,6 +119,35 @@ __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int c
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       if (col + i < n) dst[i] = D::from_f(o[i]);
+  }
+}
+
+// RoPE of the 32 accumulator columns [col, col + 32) of row `row`, all inside one q or
+// k head: each value is first rounded to the output dtype (the value the projection
+// stores, which the reference's RoPE kernel then reads, tinker/kernels/fused_attention.py
+// :53-69), then each interleaved pair (x0, x1) becomes (x0 c - x1 s, x0 s + x1 c) in fp32
+// with the angle of pair (col mod head_dim) / 2 at the row's position; the caller rounds
+// the result once more when it stores it.
+template <int DT>
+__device__ __forceinline__ void rope_chunk32(float (&v)[32], int row, int col, const Params& p) {
+  using D = Dt<DT>;
+  const int64_t pos = static_cast<int64_t>(p.rope_start) + row % p.rope_seq;
+  const int i0 = (col % (2 * p.rope_half_d)) >> 1;  // multiple of 16
+  const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + pos * p.rope_half_d + i0);
+  const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + pos * p.rope_half_d + i0);
+  float c[16], s[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 a = c4[q], b = s4[q];
+    c[4 * q] = a.x; c[4 * q + 1] = a.y; c[4 * q + 2] = a.z; c[4 * q + 3] = a.w;
+    s[4 * q] = b.x; s[4 * q + 1] = b.y; s[4 * q + 2] = b.z; s[4 * q + 3] = b.w;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x0 = D::to_f(D::from_f(v[2 * i]));
+    const float x1 = D::to_f(D::from_f(v[2 * i + 1]));
+    v[2 * i] = x0 * c[i] - x1 * s[i];
+    v[2 * i + 1] = x0 * s[i] + x1 * c[i];
   }
 }
 
@@ -302,6 +337,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
+          if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
         }
       }
@@ -494,6 +530,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
+          if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
         }
       }
@@ -735,6 +772,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[4 * j] += a.x; v[4 * j + 1] += a.y; v[4 * j + 2] += a.z; v[4 * j + 3] += a.w;
           }
         }
+        if (mine && nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
         if (mine && row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
       }
     }
@@ -935,9 +973,16 @@ static int pick_bn(int64_t m_tiles, int64_t n, int sms, const int* cands, int nc
   return 0;
 }
 
+struct RopeArgs {
+  int cols = 0, seq = 1, start = 0, half_d = 0;
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+};
+
 template <int DT>
 int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const void* w1, int64_t n1, const void* w2,
-               int64_t n2, void* y, int64_t ldy, const void* residual, int64_t m, int64_t k, cudaStream_t st) {
+               int64_t n2, void* y, int64_t ldy, const void* residual, int64_t m, int64_t k, cudaStream_t st,
+               const RopeArgs& rope = RopeArgs{}) {
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
   const int64_t n = n0 + n1 + n2;
@@ -965,6 +1010,12 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   p.y = y;
   p.ldy = ldy;
   p.residual = residual;
+  p.rope_cols = rope.cols;
+  p.rope_seq = rope.seq;
+  p.rope_start = rope.start;
+  p.rope_half_d = rope.half_d;
+  p.rope_cos = rope.cos_t;
+  p.rope_sin = rope.sin_t;
   CUtensorMap ta, tb0, tb1, tb2;
   if (int rc = tensor_map_2d(&ta, x, DT, m, k, lda, BM, BK)) return rc;
   if (int rc = tensor_map_2d(&tb0, w0, DT, n0, k, k, bn, BK)) return rc;
@@ -1110,6 +1161,37 @@ extern "C" int tk_linear(const void* x, int64_t x_row_stride, const void* w0, in
   if (dtype == TK_F16)
     return gemm::run_linear<TK_F16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
   return gemm::run_linear<TK_BF16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
+}
+
+extern "C" int tk_linear_rope(const void* x, int64_t x_row_stride, const void* wq, int64_t nq, const void* wk,
+                              int64_t nk, const void* wv, int64_t nv, void* y, int64_t y_row_stride, int64_t m,
+                              int64_t k, int seq, int start_pos, int head_dim, const void* cos_table,
+                              const void* sin_table, int64_t table_rows, int dtype, void* stream) {
+  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
+  if (head_dim <= 0 || head_dim % 32 != 0) return fail_invalid("linear_rope: head_dim must be a positive multiple of 32");
+  if (nq <= 0 || nk <= 0 || nv <= 0 || nq % head_dim != 0 || nk % head_dim != 0 || nv % 32 != 0)
+    return fail_invalid("linear_rope: q and k widths must be multiples of head_dim, v a multiple of 32");
+  if (seq <= 0 || start_pos < 0 || m % seq != 0) return fail_invalid("linear_rope: m must be a multiple of seq > 0");
+  if (int64_t(start_pos) + seq > table_rows)
+    return fail_invalid("linear_rope: start_pos + seq exceeds the RoPE table length");
+  if (m == 0) return TK_OK;
+  if (!wq || !wk || !wv) return fail_invalid("linear_rope: NULL weight");
+  if (!cos_table || !sin_table || !aligned16(cos_table) || !aligned16(sin_table))
+    return fail_invalid("linear_rope: RoPE tables must be non-NULL and 16-byte aligned");
+  const int64_t n = nq + nk + nv;
+  if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear_rope: bad output or stride");
+  if (n > INT32_MAX || m > INT32_MAX) return fail_invalid("linear_rope: too large");
+  gemm::RopeArgs r;
+  r.cols = static_cast<int>(nq + nk);
+  r.seq = seq;
+  r.start = start_pos;
+  r.half_d = head_dim / 2;
+  r.cos_t = static_cast<const float*>(cos_table);
+  r.sin_t = static_cast<const float*>(sin_table);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return gemm::run_linear<TK_F16>(x, x_row_stride, wq, nq, wk, nk, wv, nv, y, y_row_stride, nullptr, m, k, st, r);
+  return gemm::run_linear<TK_BF16>(x, x_row_stride, wq, nq, wk, nk, wv, nv, y, y_row_stride, nullptr, m, k, st, r);
 }
 
 extern "C" int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,

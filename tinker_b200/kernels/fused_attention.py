@@ -69,3 +69,22 @@ def fused_attention(q, k, v, cos_table, sin_table, num_heads, num_kv_heads, head
             num_kv_heads, head_dim, int(start_pos), _lib.dtype_code(q.dtype), _lib.stream_ptr(dev)),
             "tk_rope_attention", 1)
     return out
+
+
+def causal_attention(q, k, v, num_heads, num_kv_heads, head_dim):
+    """GQA causal attention on q and k that already carry RoPE (``linear_rope`` output slices):
+    the kernel of ``fused_attention`` without the rotation. Same shapes and result layout."""
+    dev = _lib.require_cuda(q, k, v)
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("causal_attention: q, k, v must all be float16 or all bfloat16")
+    B, S = q.shape[0], q.shape[1]
+    q3, qs = _token_stride(q, B, S, num_heads * head_dim)
+    k3, ks = _token_stride(k, B, S, num_kv_heads * head_dim)
+    v3, vs = _token_stride(v, B, S, num_kv_heads * head_dim)
+    out = torch.empty(B, S, num_heads * head_dim, dtype=q.dtype, device=q.device)
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_causal_attention(
+            q3.data_ptr(), qs, k3.data_ptr(), ks, v3.data_ptr(), vs, out.data_ptr(), num_heads * head_dim, B, S,
+            num_heads, num_kv_heads, head_dim, _lib.dtype_code(q.dtype), _lib.stream_ptr(dev)),
+            "tk_causal_attention", 1)
+    return out

@@ -7,6 +7,8 @@ tinker/modules/feed_forward.py:27-30). Here they are hand-written sm_100a GEMMs:
 * ``linear(x, w0, w1=None, w2=None, residual=None)`` - ``x @ cat(w0, w1, w2).T``
   without materialising the concatenation (the fused q|k|v projection), with an
   optional residual add in the epilogue.
+* ``linear_rope(x, wq, wk, wv, cos, sin, head_dim, start_pos)`` - the q|k|v projection with
+  RoPE applied to the q and k columns in the epilogue.
 * ``gate_up_swiglu(x, w_gate, w_up)`` - ``silu(x @ w_gate.T) * (x @ w_up.T)`` as one
   GEMM with the SwiGLU applied to the fp32 accumulators.
 * ``swiglu_ffn(x, w_gate, w_up, w_down, residual=None)`` - the whole FFN.
@@ -64,6 +66,33 @@ def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2
                                         rows[2], out.data_ptr(), n, None if r is None else r.data_ptr(), m, k,
                                         _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear", 1)
     return out.reshape(*lead, n)
+
+
+def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, cos_table: torch.Tensor,
+                sin_table: torch.Tensor, head_dim: int, start_pos: int = 0) -> torch.Tensor:
+    """``x @ cat([wq, wk, wv]).T`` for x [batch, seq, hidden] with RoPE applied to the q and k
+    columns in the GEMM epilogue (each value rounded to the output dtype, then rotated in fp32 at
+    position ``start_pos + s``): the q|k|v projection plus the RoPE of ``fused_attention``."""
+    dev = _lib.require_cuda(x, wq, wk, wv, cos_table, sin_table)
+    if x.dim() != 3:
+        raise ValueError("linear_rope: x must be [batch, seq, hidden]")
+    if cos_table.dtype != torch.float32 or sin_table.dtype != torch.float32:
+        raise TypeError("linear_rope: RoPE tables must be float32")
+    B, S, k = x.shape
+    x2 = _check_x(x)
+    wq, wk, wv = (_check_w(w, k, x.dtype) for w in (wq, wk, wv))
+    c, s_ = cos_table.contiguous(), sin_table.contiguous()
+    if c.shape != s_.shape or c.dim() != 2 or c.shape[1] != head_dim // 2:
+        raise ValueError(f"RoPE tables must be [max_seq_len, {head_dim // 2}], got {tuple(c.shape)}")
+    n = wq.shape[0] + wk.shape[0] + wv.shape[0]
+    m = x2.shape[0]
+    out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_linear_rope(
+            x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0], wv.data_ptr(),
+            wv.shape[0], out.data_ptr(), n, m, k, S, int(start_pos), head_dim, c.data_ptr(), s_.data_ptr(),
+            c.shape[0], _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear_rope", 1)
+    return out.reshape(B, S, n)
 
 
 def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:

@@ -1,8 +1,10 @@
 """fused attention module (drop-in for eb1386/TinKer tinker/modules/attention.py:9-153).
 
 ``forward`` runs three kernels: the q|k|v projection as one tcgen05 GEMM over
-the three weights (no concatenated copy), the RoPE + GQA causal attention
-reading q/k/v in place from that output, and the o_proj GEMM. The
+the three weights (no concatenated copy) whose epilogue applies RoPE to the q
+and k columns, the GQA causal attention reading q/k/v in place from that
+output, and the o_proj GEMM. (Half-precision RoPE tables take the
+``fused_attention`` path instead, which rotates on load inside attention.) The
 ``q_proj`` / ``k_proj`` / ``v_proj`` / ``o_proj`` submodules keep the reference's
 names and shapes. The RoPE tables stay float32 when the module is cast to a
 half dtype (the reference's ``model.to(dtype)`` rounds them to the model
@@ -12,8 +14,8 @@ dtype); positions are rotated with the exact float32 angles.
 import torch
 import torch.nn as nn
 
-from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
-from tinker_b200.kernels.gemm import linear
+from tinker_b200.kernels.fused_attention import causal_attention, fused_attention, precompute_rope_tables
+from tinker_b200.kernels.gemm import linear, linear_rope
 
 
 class TinKerAttention(nn.Module):
@@ -69,6 +71,14 @@ class TinKerAttention(nn.Module):
         """forward pass; with ``residual`` the o_proj epilogue adds it to the output."""
         hq = self.num_heads * self.head_dim
         hkv = self.num_kv_heads * self.head_dim
+        if (x.dim() == 3 and self.cos_table.dtype == torch.float32 and self.sin_table.dtype == torch.float32
+                and self.head_dim % 32 == 0 and hq % self.head_dim == 0):
+            # RoPE in the projection epilogue, attention on the rotated q/k
+            qkv = linear_rope(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
+                              self.cos_table, self.sin_table, self.head_dim, start_pos)
+            attn_out = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:],
+                                        self.num_heads, self.num_kv_heads, self.head_dim)
+            return linear(attn_out, self.o_proj.weight, residual=residual)
         qkv = linear(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
         q = qkv[..., :hq]
         k = qkv[..., hq:hq + hkv]
