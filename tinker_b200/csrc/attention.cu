@@ -31,40 +31,43 @@
 namespace tk {
 namespace attn {
 
-constexpr int BQ = 128;
-constexpr int BKV = 128;
-constexpr int THREADS = 320;  // warps 0-3 softmax, 4 TMA, 5 MMA, 6-9 RoPE of K (one row per thread)
-constexpr int ROPE_K_THREADS = 128;
+constexpr int BQ = 128;   // query rows per softmax warpgroup (one tcgen05 M=128 tile)
+constexpr int BKV = 128;  // keys per K/V tile
+constexpr int SOFTMAX_THREADS = 256;  // warps 0-3: query tile a, warps 4-7: query tile b
+constexpr int TMA_WARP = 8;
+constexpr int MMA_WARP = 9;
+constexpr int ROPE_WARP0 = 10;       // warps 10-11 rotate the K tiles (two rows per thread)
+constexpr int ROPE_K_THREADS = 64;
 constexpr float LAZY_RESCALE_LOG2 = 8.0f;  // move the running max only when it grows by more than 2^8
+
+__host__ __device__ constexpr int threads_for(bool rope) { return rope ? 384 : 320; }
 
 template <int D>
 struct Smem {
-  static constexpr int Q_BYTES = BQ * D * 2;
-  static constexpr int K_BYTES = BKV * D * 2;
-  static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int P_BYTES = BQ * BKV * 2;
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + Q_BYTES;      // two stages
-  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;  // two stages
-  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  static constexpr int NUM_BARS = 16;
+  static constexpr int Q_BYTES = BQ * D * 2;      // one query tile
+  static constexpr int T_BYTES = BKV * D * 2;     // one K or V tile
+  static constexpr int STAGES = D == 64 ? 4 : 3;  // K/V ring: K_0, V_0, K_1, V_1, ... through STAGES slots
+  static constexpr int P_BYTES = BQ * BKV * 2;    // one P tile
+  static constexpr int Q_OFF = 0;                 // Q_a, Q_b
+  static constexpr int RING_OFF = Q_OFF + 2 * Q_BYTES;
+  static constexpr int P_OFF = RING_OFF + STAGES * T_BYTES;  // P_a, P_b
+  static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
+  static constexpr int NUM_BARS = 24;
   static constexpr int TOTAL = 1024 + BAR_OFF + NUM_BARS * 8 + 16;
-  static constexpr uint32_t TMEM_COLS = 512;  // S0: 0-127, S1: 128-255, O: 256..256+head_dim
+  // S_a: 0-127, S_b: 128-255, O_a: 256.., O_b: 256 + head_dim..
+  static constexpr uint32_t TMEM_COLS = 512;
 };
 
 // mbarrier slots
 enum : int {
-  B_Q_FULL = 0,    // Q tile landed (TMA transaction bytes)
-  B_Q_READY = 1,   // Q rotated (128 softmax threads)
-  B_K_FULL = 2,    // [2] K stage landed
-  B_V_FULL = 4,    // [2] V stage landed
-  B_K_READY = 6,   // [2] K stage rotated (128 RoPE threads)
-  B_KV_EMPTY = 8,  // [2] S and P.V of the stage finished (UMMA commit)
-  B_S_FULL = 10,   // [2] S buffer written (UMMA commit)
-  B_S_FREE = 12,   // [2] S buffer read into registers (128 softmax threads)
-  B_P_FULL = 14,   // P written and O rescaled (128 softmax threads)
-  B_PV_DONE = 15,  // P.V finished (UMMA commit)
+  B_Q_FULL = 0,    // both Q tiles landed (TMA transaction bytes)
+  B_Q_READY = 1,   // Q tiles rotated (256 softmax threads)
+  B_FULL = 2,      // [4] ring slot landed
+  B_EMPTY = 6,     // [4] ring slot consumed (UMMA commit)
+  B_K_READY = 10,  // [2] K_j rotated, indexed by j & 1 (64 RoPE threads)
+  B_S_FULL = 12,   // [2] S_a / S_b written (UMMA commit)
+  B_P_FULL = 14,   // [2] P_a / P_b written and O rescaled (128 threads of the warpgroup)
+  B_PV_DONE = 16,  // [2] P.V of a / b finished (UMMA commit)
 };
 
 struct Params {
@@ -95,6 +98,14 @@ __device__ __forceinline__ void load_cs4(const void* t, int dt, int64_t off, flo
       v[2 * i + 1] = p.y;
     }
   }
+}
+
+// 2^x with the MUFU.EX2 approximation (PTX ex2.approx.ftz.f32; 2^-inf = +0). The
+// probabilities are rounded to 16 bits right after, far coarser than its error.
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // RoPE of one row of a swizzled [128 x D] tile, in 64-column blocks: the 32 cos and
@@ -141,46 +152,47 @@ __device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int64_t p
 }
 
 template <int DT, int D, bool ROPE>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(threads_for(ROPE), 1)
     rope_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const Params p) {
   using S = Smem<D>;
   using Dx = Dt<DT>;
+  constexpr int NS = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem + S::Q_OFF;
-  uint8_t* sk = smem + S::K_OFF;
-  uint8_t* sv = smem + S::V_OFF;
-  uint8_t* sp = smem + S::P_OFF;
+  uint8_t* ring = smem + S::RING_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NUM_BARS);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
+  // CTA = query tiles a = 2*blk and b = 2*blk + 1 of one (batch, head); heaviest pairs first
+  const int n_pairs = (p.n_qtiles + 1) >> 1;
+  const int blk = n_pairs - 1 - static_cast<int>(blockIdx.x);
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int kvh = h / p.groups;
-  const int q0 = qt * BQ;
-  const int n_kv = qt + 1;  // causal: key tiles 0..qt
+  const bool has_b = 2 * blk + 1 < p.n_qtiles;
+  const int n_a = 2 * blk + 1;             // key tiles of query tile a (causal)
+  const int n_kv = has_b ? n_a + 1 : n_a;  // key tiles loaded (query tile b needs one more)
 
   if (tid == 0) {
     mbar_init(bars + B_Q_FULL, 1);
-    mbar_init(bars + B_Q_READY, 128);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bars + B_K_FULL + i, 1);
-      mbar_init(bars + B_V_FULL + i, 1);
-      mbar_init(bars + B_K_READY + i, ROPE_K_THREADS);
-      mbar_init(bars + B_KV_EMPTY + i, 1);
-      mbar_init(bars + B_S_FULL + i, 1);
-      mbar_init(bars + B_S_FREE + i, 128);
+    mbar_init(bars + B_Q_READY, SOFTMAX_THREADS);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bars + B_FULL + i, 1);
+      mbar_init(bars + B_EMPTY + i, 1);
     }
-    mbar_init(bars + B_P_FULL, 128);
-    mbar_init(bars + B_PV_DONE, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bars + B_K_READY + i, ROPE_K_THREADS);
+      mbar_init(bars + B_S_FULL + i, 1);
+      mbar_init(bars + B_P_FULL + i, 128);
+      mbar_init(bars + B_PV_DONE + i, 1);
+    }
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
@@ -188,163 +200,215 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t t_o = tmem_base + 256;
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == TMA_WARP) {
+    // ---------------- TMA producer: Q_a|Q_b, then K_0, V_0, K_1, V_1, ... ----------------
     if (lane == 0) {
       pdl_launch_dependents();
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       pdl_wait();  // q, k, v are written by the previous kernel
-      mbar_arrive_expect_tx(bars + B_Q_FULL, S::Q_BYTES);
+      mbar_arrive_expect_tx(bars + B_Q_FULL, (has_b ? 2 : 1) * S::Q_BYTES);
+      for (int t = 0; t < (has_b ? 2 : 1); ++t)
 #pragma unroll
-      for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(sq + blk * 128 * 128, &tq, bars + B_Q_FULL, h * D + blk * 64, q0, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(bars + B_KV_EMPTY + st, ((j >> 1) - 1) & 1)) break;
-        uint8_t* k_dst = sk + st * S::K_BYTES;
-        uint8_t* v_dst = sv + st * S::V_BYTES;
-        mbar_arrive_expect_tx(bars + B_K_FULL + st, S::K_BYTES);
+        for (int cb = 0; cb < D / 64; ++cb)
+          tma_load_3d(smem + S::Q_OFF + t * S::Q_BYTES + cb * 128 * 128, &tq, bars + B_Q_FULL, h * D + cb * 64,
+                      (2 * blk + t) * BQ, b);
+      for (int i = 0; i < 2 * n_kv; ++i) {
+        const int slot = i % NS;
+        if (i >= NS && !mbar_wait(bars + B_EMPTY + slot, ((i / NS) - 1) & 1)) break;
+        const CUtensorMap* m = (i & 1) ? &tv : &tk;
+        uint8_t* dst = ring + slot * S::T_BYTES;
+        mbar_arrive_expect_tx(bars + B_FULL + slot, S::T_BYTES);
 #pragma unroll
-        for (int blk = 0; blk < D / 64; ++blk)
-          tma_load_3d(k_dst + blk * 128 * 128, &tk, bars + B_K_FULL + st, kvh * D + blk * 64, j * BKV, b);
-        mbar_arrive_expect_tx(bars + B_V_FULL + st, S::V_BYTES);
-#pragma unroll
-        for (int blk = 0; blk < D / 64; ++blk)
-          tma_load_3d(v_dst + blk * 128 * 128, &tv, bars + B_V_FULL + st, kvh * D + blk * 64, j * BKV, b);
+        for (int cb = 0; cb < D / 64; ++cb)
+          tma_load_3d(dst + cb * 128 * 128, m, bars + B_FULL + slot, kvh * D + cb * 64, (i >> 1) * BKV, b);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == MMA_WARP) {
     // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(Dx::umma_fmt, BQ, BKV, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_f16(Dx::umma_fmt, BQ, D, 0, 1);
-      // without RoPE the MMA reads the Q and K tiles as TMA lands them
-      bool ok = mbar_wait(bars + (ROPE ? B_Q_READY : B_Q_FULL), 0);
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          const int st = j & 1;
-          if (!mbar_wait(bars + (ROPE ? B_K_READY : B_K_FULL) + st, (j >> 1) & 1)) break;
-          if (j >= 2 && !mbar_wait(bars + B_S_FREE + st, ((j >> 1) - 1) & 1)) break;
-          tc_fence_after();
-          const uint32_t k_base = smem_u32(sk + st * S::K_BYTES);
+      const uint32_t q_a = smem_u32(smem + S::Q_OFF), q_b = q_a + S::Q_BYTES;
+      const uint32_t p_a = smem_u32(smem + S::P_OFF), p_b = p_a + S::P_BYTES;
+      auto issue_s = [&](uint32_t q_base, uint32_t k_base, uint32_t t_s) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-            umma_f16_ss(tmem_base + st * 128, make_sw128_desc(smem_u32(sq) + off, 0, 1024),
-                        make_sw128_desc(k_base + off, 0, 1024), idesc_s, kk != 0);
-          }
-          umma_commit(bars + B_S_FULL + st);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          umma_f16_ss(t_s, make_sw128_desc(q_base + off, 0, 1024), make_sw128_desc(k_base + off, 0, 1024), idesc_s,
+                      kk != 0);
         }
-        if (j >= 1) {
-          const int i = j - 1;
-          const int si = i & 1;
-          if (!mbar_wait(bars + B_P_FULL, i & 1)) break;
-          if (!mbar_wait(bars + B_V_FULL + si, (i >> 1) & 1)) break;
-          tc_fence_after();
-          const uint32_t v_base = smem_u32(sv + si * S::V_BYTES);
+      };
+      auto issue_pv = [&](uint32_t p_base, uint32_t v_base, uint32_t t_o, bool acc) {
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-            umma_f16_ss(t_o, make_sw128_desc(smem_u32(sp) + aoff, 0, 1024),
-                        make_sw128_desc(v_base + kk * 16 * 128, BKV * 128, 1024), idesc_o,
-                        (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          umma_f16_ss(t_o, make_sw128_desc(p_base + aoff, 0, 1024),
+                      make_sw128_desc(v_base + kk * 16 * 128, BKV * 128, 1024), idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      // K_j is ring item 2j, V_j item 2j + 1
+      auto wait_k = [&](int j) -> bool {
+        if constexpr (ROPE) return mbar_wait(bars + B_K_READY + (j & 1), (j >> 1) & 1);
+        const int i = 2 * j;
+        return mbar_wait(bars + B_FULL + i % NS, (i / NS) & 1);
+      };
+      auto slot_addr = [&](int i) { return smem_u32(ring + (i % NS) * S::T_BYTES); };
+      const uint32_t t_sa = tmem_base, t_sb = tmem_base + 128;
+      const uint32_t t_oa = tmem_base + 256, t_ob = tmem_base + 256 + D;
+
+      bool ok = mbar_wait(bars + B_Q_READY, 0) && wait_k(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(q_a, slot_addr(0), t_sa);
+        umma_commit(bars + B_S_FULL + 0);
+        if (has_b) {
+          issue_s(q_b, slot_addr(0), t_sb);
+          umma_commit(bars + B_S_FULL + 1);
+        }
+        umma_commit(bars + B_EMPTY + 0);  // K_0 consumed
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int iv = 2 * j + 1;
+        if (!mbar_wait(bars + B_FULL + iv % NS, (iv / NS) & 1)) break;
+        if (j < n_a) {
+          if (!mbar_wait(bars + B_P_FULL + 0, j & 1)) break;
+          tc_fence_after();
+          issue_pv(p_a, slot_addr(iv), t_oa, j > 0);
+          umma_commit(bars + B_PV_DONE + 0);
+        }
+        const bool next_k = j + 1 < n_kv;
+        if (next_k && !wait_k(j + 1)) break;
+        tc_fence_after();
+        if (j + 1 < n_a) {  // S_a is free: softmax a read it before publishing P_a
+          issue_s(q_a, slot_addr(iv + 1), t_sa);
+          umma_commit(bars + B_S_FULL + 0);
+        }
+        if (has_b) {
+          if (!mbar_wait(bars + B_P_FULL + 1, j & 1)) break;
+          tc_fence_after();
+          issue_pv(p_b, slot_addr(iv), t_ob, j > 0);
+          umma_commit(bars + B_PV_DONE + 1);
+        }
+        umma_commit(bars + B_EMPTY + iv % NS);  // V_j consumed
+        if (next_k) {
+          if (has_b) {
+            issue_s(q_b, slot_addr(iv + 1), t_sb);
+            umma_commit(bars + B_S_FULL + 1);
           }
-          umma_commit(bars + B_PV_DONE);
-          umma_commit(bars + B_KV_EMPTY + si);
+          umma_commit(bars + B_EMPTY + (iv + 1) % NS);  // K_{j+1} consumed
         }
       }
     }
-  } else if (warp >= 6) {
-    // ---------------- RoPE of the K stages (thread = key row) ----------------
+  } else if (warp >= ROPE_WARP0) {
+    // ---------------- RoPE of the K tiles (rows t and t + 64) ----------------
     if constexpr (ROPE) {
-      const int t = tid - 6 * 32;
+      const int t = tid - ROPE_WARP0 * 32;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const int k_row = j * BKV + t;  // rows past the sequence are zero-filled by TMA and left alone
-        const bool valid = k_row < p.seq;
-        const int64_t kpos = static_cast<int64_t>(p.start_pos) + k_row;
+        const int i = 2 * j;
+        uint8_t* kt = ring + (i % NS) * S::T_BYTES;
+        const int64_t pos0 = static_cast<int64_t>(p.start_pos) + j * BKV + t;
+        const bool v0 = j * BKV + t < p.seq, v1 = j * BKV + t + 64 < p.seq;
         float c[32], sn[32];
-        if (valid) rope_load_block(p, kpos, 0, D / 2, c, sn);  // in flight while the K tile lands
-        if (!mbar_wait(bars + B_K_FULL + st, (j >> 1) & 1)) break;
-        uint8_t* ks_ = sk + st * S::K_BYTES;
-        if (valid) {
-          rope_apply_block<DT>(ks_, t, 0, c, sn);
+        if (v0) rope_load_block(p, pos0, 0, D / 2, c, sn);  // in flight while the K tile lands
+        if (!mbar_wait(bars + B_FULL + i % NS, (i / NS) & 1)) break;
+        // rows past the sequence are zero-filled by TMA and left alone
+        if (v0) {
+          rope_apply_block<DT>(kt, t, 0, c, sn);
 #pragma unroll
-          for (int blk = 1; blk < D / 64; ++blk) {
-            rope_load_block(p, kpos, blk, D / 2, c, sn);
-            rope_apply_block<DT>(ks_, t, blk, c, sn);
+          for (int cb = 1; cb < D / 64; ++cb) {
+            rope_load_block(p, pos0, cb, D / 2, c, sn);
+            rope_apply_block<DT>(kt, t, cb, c, sn);
+          }
+        }
+        if (v1) {
+#pragma unroll
+          for (int cb = 0; cb < D / 64; ++cb) {
+            rope_load_block(p, pos0 + 64, cb, D / 2, c, sn);
+            rope_apply_block<DT>(kt, t + 64, cb, c, sn);
           }
         }
         fence_proxy_async_smem();
-        mbar_arrive(bars + B_K_READY + st);
+        mbar_arrive(bars + B_K_READY + (j & 1));
       }
     }
-  } else {
-    // ---------------- softmax / correction / output (thread = query row) ----------------
-    const int q_row = q0 + tid;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  } else if (warp < 8) {
+    // ---------------- softmax / correction / output: warpgroup x, thread = query row ----------------
+    const int x = warp >> 2;
+    const int r = tid & 127;
+    const int qt = 2 * blk + x;
+    const int q_row = qt * BQ + r;
+    const bool active = x == 0 || has_b;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem_base + x * 128;
+    const uint32_t t_o = tmem_base + 256 + x * D;
+    uint8_t* sq = smem + S::Q_OFF + x * S::Q_BYTES;
+    uint8_t* sp = smem + S::P_OFF + x * S::P_BYTES;
     bool ok = true;
     if constexpr (ROPE) {
       const int64_t qpos = static_cast<int64_t>(p.start_pos) + q_row;
-      const bool valid = q_row < p.seq;
+      const bool valid = active && q_row < p.seq;
       float c[32], sn[32];
       if (valid) rope_load_block(p, qpos, 0, D / 2, c, sn);  // in flight while the Q tile lands
       ok = mbar_wait(bars + B_Q_FULL, 0);
       if (ok && valid) {
-        rope_apply_block<DT>(sq, tid, 0, c, sn);
+        rope_apply_block<DT>(sq, r, 0, c, sn);
 #pragma unroll
-        for (int blk = 1; blk < D / 64; ++blk) {
-          rope_load_block(p, qpos, blk, D / 2, c, sn);
-          rope_apply_block<DT>(sq, tid, blk, c, sn);
+        for (int cb = 1; cb < D / 64; ++cb) {
+          rope_load_block(p, qpos, cb, D / 2, c, sn);
+          rope_apply_block<DT>(sq, r, cb, c, sn);
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(bars + B_Q_READY);
     }
+    mbar_arrive(bars + B_Q_READY);
 
+    const int n_x = x == 0 ? n_a : n_a + 1;
     float m_run = -INFINITY, l_run = 0.f;
-    for (int j = 0; ok && j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(bars + B_S_FULL + sb, (j >> 1) & 1)) { ok = false; break; }
+    for (int j = 0; active && ok && j < n_x; ++j) {
+      if (!mbar_wait(bars + B_S_FULL + x, j & 1)) { ok = false; break; }
       tc_fence_after();
-      float s[BKV];
+      float sv[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 32)
-        tmem_ld32(tmem_base + sb * 128 + lane_off + c, *reinterpret_cast<float(*)[32]>(&s[c]));
+      for (int c = 0; c < BKV; c += 32) tmem_ld32(t_s + lane_off + c, *reinterpret_cast<float(*)[32]>(&sv[c]));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bars + B_S_FREE + sb);
 
-      const bool diag = (j == qt);
-      float mx = -INFINITY;
+      // mask the diagonal tile, then the row maximum over eight independent chains
+      if (j == qt) {
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        float v = s[c] * p.scale_log2;
-        if (diag && (j * BKV + c) > q_row) v = -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < BKV; ++c)
+          if (j * BKV + c > q_row) sv[c] = -INFINITY;
       }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < BKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
       // lazy rescale: keep the old maximum unless this tile exceeds it by more than 2^8
       float m_use = m_run, alpha = 1.f;
       if (mx > m_run + LAZY_RESCALE_LOG2) {
         m_use = mx;
-        alpha = exp2f(m_run - mx);
+        alpha = exp2_approx(m_run - mx);
       }
-      float rs = 0.f;
+      // p = 2^(s * scale * log2(e) - m): one FMA and one MUFU.EX2 per score
+      const float neg_m = -m_use;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
-        s[c] = exp2f(s[c] - m_use);
-        rs += s[c];
+        sv[c] = exp2_approx(fmaf(sv[c], p.scale_log2, neg_m));
+        rs8[c & 7] += sv[c];
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l_run = l_run * alpha + rs;
       m_run = m_use;
 
       if (j > 0) {
         // P and the O accumulator are still in use by the previous P.V
-        if (!mbar_wait(bars + B_PV_DONE, (j - 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(bars + B_PV_DONE + x, (j - 1) & 1)) { ok = false; break; }
         tc_fence_after();
       }
 #pragma unroll
@@ -352,10 +416,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          typename Dx::T2 hv = Dx::pack(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
+          typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
           w[i] = *reinterpret_cast<uint32_t*>(&hv);
         }
-        uint8_t* dst = sp + (c >> 3) * (128 * 128) + tid * 128 + (((c & 7) ^ (tid & 7)) * 16);
+        uint8_t* dst = sp + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) * 16);
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -372,10 +436,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bars + B_P_FULL);
+      mbar_arrive(bars + B_P_FULL + x);
     }
 
-    if (ok && mbar_wait(bars + B_PV_DONE, (n_kv - 1) & 1)) {
+    if (active && ok && mbar_wait(bars + B_PV_DONE + x, (n_x - 1) & 1)) {
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
       using T = typename Dx::T;
@@ -404,7 +468,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
@@ -429,7 +493,7 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
       return rc;
     configured[dev.device] = true;
   }
-  return launch_kernel(kern, dim3(p.n_qtiles, p.num_heads, p.batch), dim3(THREADS), S::TOTAL, st, 1,
+  return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(threads_for(ROPE)), S::TOTAL, st, 1,
                        ROPE ? "rope_attention_kernel" : "causal_attention_kernel", tq, tk_, tv, p);
 }
 
