@@ -371,9 +371,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       if (!mbar_wait(bars + B_S_FULL + x, j & 1)) { ok = false; break; }
       tc_fence_after();
       float sv[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV; c += 32) tmem_ld32(t_s + lane_off + c, *reinterpret_cast<float(*)[32]>(&sv[c]));
-      tmem_wait_ld();
+      tmem_load128(t_s + lane_off, sv);
 
       // mask the diagonal tile, then the row maximum over eight independent chains
       if (j == qt) {
@@ -426,13 +424,11 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
 #pragma unroll
         for (int c = 0; c < D; c += 32) {
           float o[32];
-          tmem_ld32(t_o + lane_off + c, o);
-          tmem_wait_ld();
+          tmem_load32(t_o + lane_off + c, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
           tmem_st32(t_o + lane_off + c, o);
         }
-        tmem_wait_st();
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -448,8 +444,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
 #pragma unroll
       for (int c = 0; c < D; c += 32) {
         float o[32];
-        tmem_ld32(t_o + lane_off + c, o);
-        tmem_wait_ld();
+        tmem_load32(t_o + lane_off + c, o);
         if (q_row < p.seq) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {

@@ -314,9 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
         // 16 gate columns followed by 16 up columns
         float g[32], u[16];
-        tmem_ld16(taddr, g);
-        tmem_ld16(taddr + BN / 2, u);
-        tmem_wait_ld();
+        tmem_load16x2(taddr, taddr + BN / 2, g, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
         if (row < p.m) store_row16<DT>(p.y, p.ldy, row, nt * (BN / 2), p.n, g);
@@ -324,9 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float g[32], u[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + BN / 2 + c, u);
-          tmem_wait_ld();
+          tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
 #pragma unroll
           for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
@@ -335,8 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
-          tmem_ld32(taddr + c, v);
-          tmem_wait_ld();
+          tmem_load32(taddr + c, v);
           if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
         }
@@ -517,9 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float g[32], u[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + BN / 2 + c, u);
-          tmem_wait_ld();
+          tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
 #pragma unroll
           for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
@@ -528,8 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
-          tmem_ld32(taddr + c, v);
-          tmem_wait_ld();
+          tmem_load32(taddr + c, v);
           if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
         }
@@ -704,8 +696,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
-        tmem_ld32(taddr + c, v);
-        tmem_wait_ld();
+        tmem_load32(taddr + c, v);
         if (owner != rank) {
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -723,9 +714,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int rstride = S::rows_owned_max(split) * S::ROW_F;
     if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
       float g[32], u[16];
-      tmem_ld16(taddr, g);
-      tmem_ld16(taddr + BN / 2, u);
-      tmem_wait_ld();
+      tmem_load16x2(taddr, taddr + BN / 2, g, u);
       for (int s2 = 0; mine && s2 < split - 1; ++s2) {
         const float* r = rbase + s2 * rstride;
 #pragma unroll
@@ -741,9 +730,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
       for (int c = 0; c < BN / 2; c += 32) {
         float g[32], u[32];
-        tmem_ld32(taddr + c, g);
-        tmem_ld32(taddr + BN / 2 + c, u);
-        tmem_wait_ld();
+        tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
         for (int s2 = 0; mine && s2 < split - 1; ++s2) {
           const float4* rg = reinterpret_cast<const float4*>(rbase + s2 * rstride + c);
           const float4* ru = reinterpret_cast<const float4*>(rbase + s2 * rstride + BN / 2 + c);
@@ -762,8 +749,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
-        tmem_ld32(taddr + c, v);
-        tmem_wait_ld();
+        tmem_load32(taddr + c, v);
         for (int s2 = 0; mine && s2 < split - 1; ++s2) {
           const float4* r = reinterpret_cast<const float4*>(rbase + s2 * rstride + c);
 #pragma unroll
