@@ -66,6 +66,16 @@ TK_API int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, i
                int64_t y_row_stride, int64_t rows, int64_t dim, float eps, int dtype, void* stream);
 
 /*
+ * Row sums of squares for an RMSNorm folded into the next GEMM (tk_epilogue.row_ssq_in):
+ * parts[(c / 32) * m + r] = sum of x[r, c .. c+31]^2 in float32, for every 32-column
+ * chunk c of k columns (k a multiple of 32). The statistics pass of
+ * _rmsnorm_kernel (tinker/kernels/fused_rmsnorm.py:12-52) without its normalisation,
+ * for rows no GEMM epilogue produced (the embedding output).
+ */
+TK_API int tk_row_sumsq(const void* x, int64_t x_row_stride, int64_t m, int64_t k, float* parts, int dtype,
+                 void* stream);
+
+/*
  * Residual add fused with RMSNorm: s = x + residual (rounded to dtype), written
  * to residual_out; y = rmsnorm(s). The residual update of the reference decoder
  * block (benchmarks/bench_e2e.py:112-115) followed by its next norm
@@ -113,6 +123,42 @@ TK_API int tk_causal_attention(const void* q, int64_t q_tok_stride, const void* 
                         int seq, int num_heads, int num_kv_heads, int head_dim, int dtype, void* stream);
 
 /*
+ * Epilogue options of tk_linear_ex / tk_gate_up_swiglu_ex (zero-initialise, then set):
+ *  residual       [m, n] with y's row stride, added before the one rounding (plain store).
+ *  row_ssq_in     [row_ssq_parts, m] float32 partial sums of squares of x's rows: the
+ *                 accumulator of row r is scaled by 1/sqrt(sum / k + row_ssq_eps), i.e. the
+ *                 GEMM consumes rmsnorm(x) whose weight has been multiplied into w's
+ *                 columns (TinKerRMSNorm + the projection that follows it,
+ *                 tinker/modules/normalization.py:29-31 then attention.py:55 /
+ *                 feed_forward.py:27-28).
+ *  row_ssq_out    plain store only: [ceil(n / 32), m] float32, the sum of squares of the
+ *                 32 stored (rounded) values of row r from column 32 j on, at [j * m + r];
+ *                 the row_ssq_in of the next folded RMSNorm.
+ *  rope_*         plain store only, rope_head_dim > 0: the columns [0, n0 + n1) (the q
+ *                 and k heads) are rounded to dtype and rotated as in tk_linear_rope.
+ */
+typedef struct tk_epilogue {
+  const void* residual;
+  const float* row_ssq_in;
+  int row_ssq_parts;
+  float row_ssq_eps;
+  float* row_ssq_out;
+  int rope_seq;
+  int rope_start;
+  int rope_head_dim;
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_table_rows;
+} tk_epilogue;
+
+/*
+ * tk_linear with the epilogue options above (NULL = plain store).
+ */
+TK_API int tk_linear_ex(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
+                 const void* w2, int64_t n2, void* y, int64_t y_row_stride, int64_t m, int64_t k,
+                 const tk_epilogue* epi, int dtype, void* stream);
+
+/*
  * y[m, n] = x[m, k] . w[n, k]^T on tcgen05 (nn.Linear without bias), fp32
  * accumulation in TMEM. Replaces the nn.Linear projections the reference's
  * modules run through cuBLAS (tinker/modules/attention.py:53-55,64;
@@ -152,6 +198,13 @@ TK_API int tk_linear_rope(const void* x, int64_t x_row_stride, const void* wq, i
  */
 TK_API int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
                       int64_t m, int64_t hidden, int64_t f, int dtype, void* stream);
+
+/*
+ * tk_gate_up_swiglu with epilogue options (only row_ssq_in / row_ssq_eps apply: the
+ * RMSNorm before the FFN folded into w_gate and w_up).
+ */
+TK_API int tk_gate_up_swiglu_ex(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
+                         int64_t m, int64_t hidden, int64_t f, const tk_epilogue* epi, int dtype, void* stream);
 
 /*
  * Whole SwiGLU FFN: out = (silu(x Wg^T) * (x Wu^T)) Wd^T (+ residual).

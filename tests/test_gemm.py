@@ -164,3 +164,92 @@ def test_pair_tiles_swiglu(dt):
     idx = torch.arange(0, m, 11, device="cuda")
     a, b = _ref(x[idx], [wg]), _ref(x[idx], [wu])
     assert rel_err(np32(h[idx]), a / (1 + np.exp(-a)) * b) <= TOL[dtype]
+
+
+# ---- RMSNorm folded into the GEMM (row_ssq_in) and row statistics out (row_ssq_out) ----
+
+def _rms_ref(x, w_norm, eps):
+    """The reference's RMSNorm in float64 on the half input, rounded like its kernel's output."""
+    xf = np32(x).astype(np.float64)
+    y = xf / np.sqrt((xf ** 2).mean(-1, keepdims=True) + eps) * np32(w_norm).astype(np.float64)
+    return y
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 5632, 1024), (300, 896, 896), (4096, 1152, 896)])
+def test_row_sumsq_and_folded_norm_linear(dt, m, n, k):
+    """row_sumsq gives the per-32-column sums of squares; linear with row_ssq_in and the norm weight
+    folded into w equals rmsnorm(x) @ w.T (tinker/modules/normalization.py:29-31 then nn.Linear)."""
+    require_b200()
+    from tinker_b200.kernels import linear, row_sumsq
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    wn = (1 + 0.1 * torch.randn(k, device="cuda", generator=g)).to(dtype)
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(dtype)
+    parts = row_sumsq(x)
+    assert parts.shape == (k // 32, m)
+    exp = (np32(x).astype(np.float64).reshape(m, k // 32, 32) ** 2).sum(-1).T
+    np.testing.assert_allclose(np32(parts), exp, rtol=1e-5, atol=1e-5)
+    wf = (w.float() * wn.float()[None, :]).to(dtype)
+    y = linear(x, wf, row_ssq_in=parts, row_ssq_eps=1e-6)
+    ref = _rms_ref(x, wn, 1e-6) @ np32(w).astype(np.float64).T
+    assert rel_err(np32(y), ref) <= 2 * TOL[dtype]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 1024, 2816), (1000, 896, 4864), (130, 96, 64)])
+def test_row_ssq_out_of_residual_linear(dt, m, n, k):
+    """row_ssq_out holds, per 32 output columns, the sum of squares of the stored (rounded) rows."""
+    require_b200()
+    from tinker_b200.kernels import linear
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(3 * m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(dtype)
+    r = torch.randn(m, n, device="cuda", generator=g).to(dtype)
+    ssq = torch.full(((n + 31) // 32, m), float("nan"), device="cuda")
+    y = linear(x, w, residual=r, row_ssq_out=ssq)
+    assert rel_err(np32(y), _ref(x, [w], r)) <= TOL[dtype]
+    yf = np32(y).astype(np.float64)
+    pad = (-n) % 32
+    exp = (np.pad(yf, ((0, 0), (0, pad))).reshape(m, -1, 32) ** 2).sum(-1).T
+    np.testing.assert_allclose(np32(ssq), exp, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("m, hidden, f", [(128, 1024, 2816), (4096, 896, 4864), (256, 512, 1376)])
+def test_folded_norm_gate_up_swiglu(dt, m, hidden, f):
+    require_b200()
+    from tinker_b200.kernels import gate_up_swiglu, row_sumsq
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(m + f)
+    x = torch.randn(m, hidden, device="cuda", generator=g).to(dtype)
+    wn = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).to(dtype)
+    wg = (0.03 * torch.randn(f, hidden, device="cuda", generator=g)).to(dtype)
+    wu = (0.03 * torch.randn(f, hidden, device="cuda", generator=g)).to(dtype)
+    fold = lambda w: (w.float() * wn.float()[None, :]).to(dtype)
+    h = gate_up_swiglu(x, fold(wg), fold(wu), row_ssq_in=row_sumsq(x), row_ssq_eps=1e-5)
+    xn = _rms_ref(x, wn, 1e-5)
+    a = xn @ np32(wg).astype(np.float64).T
+    b = xn @ np32(wu).astype(np.float64).T
+    assert rel_err(np32(h), a / (1 + np.exp(-a)) * b) <= 2 * TOL[dtype]
+
+
+def test_folded_norm_arguments_rejected():
+    require_b200()
+    from tinker_b200 import _lib
+    from tinker_b200.kernels import gate_up_swiglu, linear
+    x = torch.randn(128, 256, device="cuda", dtype=torch.float16)
+    w = torch.randn(64, 256, device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError, match="row_ssq_in"):
+        linear(x, w, row_ssq_in=torch.zeros(8, 100, device="cuda"))
+    with pytest.raises(ValueError, match="row_ssq_out"):
+        linear(x, w, row_ssq_out=torch.zeros(3, 128, device="cuda"))
+    # the SwiGLU epilogue stores h, not the rows a next RMSNorm would read
+    e = _lib.Epilogue()
+    e.row_ssq_out = torch.zeros(4, 128, device="cuda").data_ptr()
+    h = torch.empty(128, 64, device="cuda", dtype=torch.float16)
+    rc = _lib.lib().tk_gate_up_swiglu_ex(x.data_ptr(), 256, w.data_ptr(), w.data_ptr(), h.data_ptr(), 128, 256, 64, e,
+                                         0, _lib.stream_ptr(x.device))
+    assert rc == _lib.TK_ERR_INVALID

@@ -129,3 +129,31 @@ def test_block_fusion_matches_unfused_and_skips_other_structures():
     wrapper = nn.Module()
     wrapper.blk = Parallel(a.layers[0])
     assert fuse_decoder_blocks(wrapper) == 0
+
+
+def test_folded_norms_match_unfolded_and_follow_weight_updates():
+    """RMSNorms folded into the q|k|v and gate|up GEMMs (5 launches per block) give the same
+    logits as norm-then-GEMM blocks, and a norm weight changed in place is folded again."""
+    require_b200()
+    import tinker_b200
+    from tinker_b200 import _lib
+    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    cfg = TINY.with_(num_layers=3)
+    tokens = make_tokens(cfg, 2, 96, seed=5).cuda()
+    a = tinker_b200.optimize(build_model(cfg, seed=8).cuda(), dtype=torch.float16, fold_norms=False)
+    b = tinker_b200.optimize(build_model(cfg, seed=8).cuda(), dtype=torch.float16, fold_norms=True)
+    with torch.inference_mode():
+        ya = a(tokens).float()
+        n0 = _lib.launch_counter[0]
+        yb = b(tokens).float()
+        launches = _lib.launch_counter[0] - n0
+    assert ((ya - yb).norm() / ya.norm()).item() < 5e-3
+    # 5 per block + row statistics of the first block's input + final norm
+    assert launches == 5 * cfg.num_layers + 2
+    with torch.no_grad():
+        for m in (a, b):
+            m.layers[1].ffn_norm.weight.mul_(1.5)
+    with torch.inference_mode():
+        ya2, yb2 = a(tokens).float(), b(tokens).float()
+    assert ((ya2 - ya).norm() / ya.norm()).item() > 1e-2
+    assert ((ya2 - yb2).norm() / ya2.norm()).item() < 5e-3

@@ -24,6 +24,17 @@ _I64 = ctypes.c_int64
 _I = ctypes.c_int
 _F = ctypes.c_float
 
+
+
+class Epilogue(ctypes.Structure):
+    """``tk_epilogue`` of tinker_b200.h: options of tk_linear_ex / tk_gate_up_swiglu_ex."""
+    _fields_ = [("residual", _P), ("row_ssq_in", _P), ("row_ssq_parts", _I), ("row_ssq_eps", _F),
+                ("row_ssq_out", _P), ("rope_seq", _I), ("rope_start", _I), ("rope_head_dim", _I),
+                ("rope_cos", _P), ("rope_sin", _P), ("rope_table_rows", _I64)]
+
+
+_EPI = ctypes.POINTER(Epilogue)
+
 # name -> argtypes; every entry point returns int (status)
 SIGNATURES = {
     "tk_version": [],
@@ -37,7 +48,10 @@ SIGNATURES = {
     "tk_linear": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _P],
     "tk_linear_rope": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I,
                        _P],
+    "tk_linear_ex": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _EPI, _I, _P],
     "tk_gate_up_swiglu": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _P],
+    "tk_gate_up_swiglu_ex": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _EPI, _I, _P],
+    "tk_row_sumsq": [_P, _I64, _I64, _I64, _P, _I, _P],
     "tk_swiglu_ffn": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_swiglu_ffn_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
 }

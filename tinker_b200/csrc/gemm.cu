@@ -51,7 +51,23 @@ struct Params {
   int rope_seq, rope_start, rope_half_d;
   const float* rope_cos;  // [table_rows, rope_half_d] float32
   const float* rope_sin;
+  // RMSNorm folded into this GEMM (its weight already multiplied into the weights): the
+  // result of row r is scaled by 1/sqrt(sum_i ssq_in[i * m + r] * ssq_inv_k + ssq_eps).
+  const float* ssq_in;   // [ssq_parts, m] partial sums of squares of x's rows, or null
+  int ssq_parts;
+  float ssq_inv_k, ssq_eps;
+  // Plain store: ssq_out[(col / 32) * m + r] = sum of squares of the 32 stored (rounded)
+  // values of row r from column col on, the input of a folded RMSNorm downstream.
+  float* ssq_out;
 };
+
+// 1/rms of input row `row` for a folded RMSNorm (1 when there is none or the row is padding).
+__device__ __forceinline__ float row_rstd(const Params& p, int row) {
+  if (!p.ssq_in || row >= p.m) return 1.f;
+  float s = 0.f;
+  for (int i = 0; i < p.ssq_parts; ++i) s += p.ssq_in[static_cast<int64_t>(i) * p.m + row];
+  return rsqrtf(s * p.ssq_inv_k + p.ssq_eps);
+}
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mt, int& nt) {
   const int per_group = GROUP_M * p.n_tiles;
@@ -75,9 +91,19 @@ struct Smem {
                                                          : (2 * BN) <= 256 ? 256 : 512;
 };
 
+// silu(g) * u in fp32, as the SwiGLU epilogue has always computed it.
+__device__ __forceinline__ float swiglu_f(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+
+__device__ __forceinline__ void scale32(float (&v)[32], float s) {
+  if (s != 1.f) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= s;
+  }
+}
+
 template <int DT>
 __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int col, int n, const float (&v)[32],
-                                            const void* residual) {
+                                            const void* residual, float* ssq = nullptr) {
   using D = Dt<DT>;
   using T = typename D::T;
   T* dst = reinterpret_cast<T*>(y) + static_cast<int64_t>(row) * ldy + col;
@@ -104,6 +130,7 @@ __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int c
         if (col + i < n) o[i] += D::to_f(r[i]);
     }
   }
+  float sq = 0.f;
   if (col + 32 <= n) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -111,6 +138,10 @@ __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int c
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         typename D::T2 h = D::pack(o[q * 8 + 2 * j], o[q * 8 + 2 * j + 1]);
+        if (ssq) {
+          const float2 r = D::unpack(h);
+          sq = fmaf(r.x, r.x, fmaf(r.y, r.y, sq));
+        }
         w[j] = *reinterpret_cast<uint32_t*>(&h);
       }
       reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -118,8 +149,19 @@ __device__ __forceinline__ void store_row32(void* y, int64_t ldy, int row, int c
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      if (col + i < n) dst[i] = D::from_f(o[i]);
+      if (col + i < n) {
+        const T t = D::from_f(o[i]);
+        dst[i] = t;
+        const float r = D::to_f(t);
+        sq = fmaf(r, r, sq);
+      }
   }
+  if (ssq) *ssq = sq;
+}
+
+// Where a plain-store epilogue puts the row sum of squares of its 32-column chunk (or null).
+__device__ __forceinline__ float* ssq_slot(const Params& p, int row, int col) {
+  return p.ssq_out ? p.ssq_out + static_cast<int64_t>(col >> 5) * p.m + row : nullptr;
 }
 
 // RoPE of the 32 accumulator columns [col, col + 32) of row `row`, all inside one q or
@@ -311,12 +353,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       const int row = mt * BM + row_in_tile;
+      const float rs = row_rstd(p, row);
       if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
         // 16 gate columns followed by 16 up columns
         float g[32], u[16];
         tmem_load16x2(taddr, taddr + BN / 2, g, u);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+        for (int j = 0; j < 16; ++j) g[j] = swiglu_f(g[j] * rs, u[j] * rs);
         if (row < p.m) store_row16<DT>(p.y, p.ldy, row, nt * (BN / 2), p.n, g);
       } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
@@ -324,7 +367,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float g[32], u[32];
           tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          for (int j = 0; j < 32; ++j) g[j] = swiglu_f(g[j] * rs, u[j] * rs);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
         }
       } else {
@@ -332,8 +375,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < BN; c += 32) {
           float v[32];
           tmem_load32(taddr + c, v);
+          scale32(v, rs);
           if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
-          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual, ssq_slot(p, row, nt * BN + c));
         }
       }
       tc_fence_before();
@@ -508,13 +552,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       const int row = mt * 256 + row_in_tile;
+      const float rs = row_rstd(p, row);
       if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float g[32], u[32];
           tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          for (int j = 0; j < 32; ++j) g[j] = swiglu_f(g[j] * rs, u[j] * rs);
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
         }
       } else {
@@ -522,8 +567,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < BN; c += 32) {
           float v[32];
           tmem_load32(taddr + c, v);
+          scale32(v, rs);
           if (nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
-          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+          if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual, ssq_slot(p, row, nt * BN + c));
         }
       }
       tc_fence_before();
@@ -710,6 +756,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp >= 2 && have_acc && __any_sync(0xffffffffu, owner == rank)) {
     const bool mine = owner == rank;
     const int row = mt * BM + quarter * 32 + lane;
+    const float rs = row_rstd(p, row);
     const float* rbase = recv + local_row * S::ROW_F;
     const int rstride = S::rows_owned_max(split) * S::ROW_F;
     if constexpr (EPI == EPI_SWIGLU && BN / 2 < 32) {
@@ -724,7 +771,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+      for (int j = 0; j < 16; ++j) g[j] = swiglu_f(g[j] * rs, u[j] * rs);
       if (mine && row < p.m) store_row16<DT>(p.y, p.ldy, row, nt * (BN / 2), p.n, g);
     } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
@@ -742,7 +789,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+        for (int j = 0; j < 32; ++j) g[j] = swiglu_f(g[j] * rs, u[j] * rs);
         if (mine && row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
       }
     } else {
@@ -758,8 +805,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[4 * j] += a.x; v[4 * j + 1] += a.y; v[4 * j + 2] += a.z; v[4 * j + 3] += a.w;
           }
         }
+        scale32(v, rs);
         if (mine && nt * BN + c < p.rope_cols) rope_chunk32<DT>(v, row, nt * BN + c, p);
-        if (mine && row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual);
+        if (mine && row < p.m)
+          store_row32<DT>(p.y, p.ldy, row, nt * BN + c, p.n, v, p.residual, ssq_slot(p, row, nt * BN + c));
       }
     }
   }
@@ -959,16 +1008,36 @@ static int pick_bn(int64_t m_tiles, int64_t n, int sms, const int* cands, int nc
   return 0;
 }
 
-struct RopeArgs {
-  int cols = 0, seq = 1, start = 0, half_d = 0;
-  const float* cos_t = nullptr;
-  const float* sin_t = nullptr;
+// Epilogue options beyond the plain store (see tk_epilogue in the header).
+struct Extras {
+  const void* residual = nullptr;
+  int rope_cols = 0, rope_seq = 1, rope_start = 0, rope_half_d = 0;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  const float* ssq_in = nullptr;
+  int ssq_parts = 0;
+  float ssq_inv_k = 0.f, ssq_eps = 0.f;
+  float* ssq_out = nullptr;
 };
+
+void apply_extras(Params& p, const Extras& e) {
+  p.residual = e.residual;
+  p.rope_cols = e.rope_cols;
+  p.rope_seq = e.rope_seq;
+  p.rope_start = e.rope_start;
+  p.rope_half_d = e.rope_half_d;
+  p.rope_cos = e.rope_cos;
+  p.rope_sin = e.rope_sin;
+  p.ssq_in = e.ssq_in;
+  p.ssq_parts = e.ssq_parts;
+  p.ssq_inv_k = e.ssq_inv_k;
+  p.ssq_eps = e.ssq_eps;
+  p.ssq_out = e.ssq_out;
+}
 
 template <int DT>
 int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const void* w1, int64_t n1, const void* w2,
-               int64_t n2, void* y, int64_t ldy, const void* residual, int64_t m, int64_t k, cudaStream_t st,
-               const RopeArgs& rope = RopeArgs{}) {
+               int64_t n2, void* y, int64_t ldy, int64_t m, int64_t k, cudaStream_t st, const Extras& ex) {
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
   const int64_t n = n0 + n1 + n2;
@@ -995,13 +1064,7 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   p.seg2 = n2 ? static_cast<int>((n0 + n1) / bn) : p.n_tiles;
   p.y = y;
   p.ldy = ldy;
-  p.residual = residual;
-  p.rope_cols = rope.cols;
-  p.rope_seq = rope.seq;
-  p.rope_start = rope.start;
-  p.rope_half_d = rope.half_d;
-  p.rope_cos = rope.cos_t;
-  p.rope_sin = rope.sin_t;
+  apply_extras(p, ex);
   CUtensorMap ta, tb0, tb1, tb2;
   if (int rc = tensor_map_2d(&ta, x, DT, m, k, lda, BM, BK)) return rc;
   if (int rc = tensor_map_2d(&tb0, w0, DT, n0, k, k, bn, BK)) return rc;
@@ -1051,7 +1114,7 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
 
 template <int DT>
 int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void* h, int64_t m, int64_t hidden,
-                int64_t f, cudaStream_t st) {
+                int64_t f, cudaStream_t st, const Extras& ex) {
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
   const int64_t m_tiles = (m + BM - 1) / BM;
@@ -1079,7 +1142,7 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
     q.seg1 = q.seg2 = q.n_tiles;
     q.y = h;
     q.ldy = f;
-    q.residual = nullptr;
+    apply_extras(q, ex);
     CUtensorMap pa, pg, pu;
     if (int rc = tensor_map_2d(&pa, x, DT, m, hidden, lda, 128, BK)) return rc;
     if (int rc = tensor_map_2d(&pg, wg, DT, f, hidden, hidden, 128, BK)) return rc;
@@ -1096,7 +1159,7 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
   p.seg1 = p.seg2 = p.n_tiles;
   p.y = h;
   p.ldy = f;
-  p.residual = nullptr;
+  apply_extras(p, ex);
   CUtensorMap ta, tg, tu;
   if (int rc = tensor_map_2d(&ta, x, DT, m, hidden, lda, BM, BK)) return rc;
   if (int rc = tensor_map_2d(&tg, wg, DT, f, hidden, hidden, half, BK)) return rc;
@@ -1132,63 +1195,109 @@ static int check_gemm_common(int dtype, const void* x, int64_t lda, int64_t m, i
   return TK_OK;
 }
 
+namespace {
+
+// Host-side checks of the epilogue options; fills the device-side Extras.
+int extras_from(const tk_epilogue* e, int64_t m, int64_t k, int64_t n, int64_t rope_cols, bool plain_store,
+                gemm::Extras* ex, const char* what) {
+  *ex = gemm::Extras{};
+  if (!e) return TK_OK;
+  if (e->residual && !plain_store) return fail_invalid("epilogue: a residual needs the plain store");
+  ex->residual = e->residual;
+  if (e->row_ssq_in) {
+    if (e->row_ssq_parts <= 0 || !(e->row_ssq_eps >= 0.f)) return fail_invalid("epilogue: bad row_ssq_parts / eps");
+    ex->ssq_in = e->row_ssq_in;
+    ex->ssq_parts = e->row_ssq_parts;
+    ex->ssq_inv_k = 1.0f / static_cast<float>(k);
+    ex->ssq_eps = e->row_ssq_eps;
+  }
+  if (e->row_ssq_out) {
+    if (!plain_store) return fail_invalid("epilogue: row_ssq_out needs the plain store");
+    ex->ssq_out = e->row_ssq_out;
+  }
+  if (e->rope_head_dim) {
+    const int hd = e->rope_head_dim;
+    if (!plain_store || hd < 32 || hd % 32 != 0 || rope_cols % hd != 0 || rope_cols > n)
+      return fail_invalid("epilogue: RoPE needs the plain store, head_dim a multiple of 32 and whole q/k heads");
+    if (e->rope_seq <= 0 || e->rope_start < 0 || m % e->rope_seq != 0)
+      return fail_invalid("epilogue: RoPE rows must be [batch, seq] tokens with seq > 0");
+    if (int64_t(e->rope_start) + e->rope_seq > e->rope_table_rows)
+      return fail_invalid("epilogue: start_pos + seq exceeds the RoPE table length");
+    if (!e->rope_cos || !e->rope_sin || !aligned16(e->rope_cos) || !aligned16(e->rope_sin))
+      return fail_invalid("epilogue: RoPE tables must be non-NULL and 16-byte aligned");
+    ex->rope_cols = static_cast<int>(rope_cols);
+    ex->rope_seq = e->rope_seq;
+    ex->rope_start = e->rope_start;
+    ex->rope_half_d = hd / 2;
+    ex->rope_cos = static_cast<const float*>(e->rope_cos);
+    ex->rope_sin = static_cast<const float*>(e->rope_sin);
+  }
+  (void)what;
+  return TK_OK;
+}
+
+}  // namespace
+
+extern "C" int tk_linear_ex(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1,
+                            int64_t n1, const void* w2, int64_t n2, void* y, int64_t y_row_stride, int64_t m,
+                            int64_t k, const tk_epilogue* epi, int dtype, void* stream) {
+  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
+  if (n0 <= 0 || n1 < 0 || n2 < 0 || (n2 && !n1)) return fail_invalid("linear: invalid weight blocks");
+  if ((n1 || n2) && (n0 % 32 != 0 || n1 % 32 != 0)) return fail_invalid("linear: weight blocks 0 and 1 must be multiples of 32 rows");
+  const int64_t n = n0 + n1 + n2;
+  if (n > INT32_MAX || m > INT32_MAX) return fail_invalid("linear: too large");
+  gemm::Extras ex;
+  if (int rc = extras_from(epi, m, k, n, n0 + n1, true, &ex, "linear")) return rc;
+  if (m == 0) return TK_OK;
+  if (!w0 || (n1 && !w1) || (n2 && !w2)) return fail_invalid("linear: NULL weight");
+  if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear: bad output or stride");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return gemm::run_linear<TK_F16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, m, k, st, ex);
+  return gemm::run_linear<TK_BF16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, m, k, st, ex);
+}
+
 extern "C" int tk_linear(const void* x, int64_t x_row_stride, const void* w0, int64_t n0, const void* w1, int64_t n1,
                          const void* w2, int64_t n2, void* y, int64_t y_row_stride, const void* residual, int64_t m,
                          int64_t k, int dtype, void* stream) {
-  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
-  if (n0 <= 0 || n1 < 0 || n2 < 0 || (n2 && !n1)) return fail_invalid("linear: invalid weight blocks");
-  if (m == 0) return TK_OK;
-  if (!w0 || (n1 && !w1) || (n2 && !w2)) return fail_invalid("linear: NULL weight");
-  if ((n1 || n2) && (n0 % 32 != 0 || n1 % 32 != 0)) return fail_invalid("linear: weight blocks 0 and 1 must be multiples of 32 rows");
-  const int64_t n = n0 + n1 + n2;
-  if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear: bad output or stride");
-  if (m == 0) return TK_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TK_F16)
-    return gemm::run_linear<TK_F16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
-  return gemm::run_linear<TK_BF16>(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, residual, m, k, st);
+  tk_epilogue e{};
+  e.residual = residual;
+  return tk_linear_ex(x, x_row_stride, w0, n0, w1, n1, w2, n2, y, y_row_stride, m, k, &e, dtype, stream);
 }
 
 extern "C" int tk_linear_rope(const void* x, int64_t x_row_stride, const void* wq, int64_t nq, const void* wk,
                               int64_t nk, const void* wv, int64_t nv, void* y, int64_t y_row_stride, int64_t m,
                               int64_t k, int seq, int start_pos, int head_dim, const void* cos_table,
                               const void* sin_table, int64_t table_rows, int dtype, void* stream) {
-  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, k)) return rc;
-  if (head_dim <= 0 || head_dim % 32 != 0) return fail_invalid("linear_rope: head_dim must be a positive multiple of 32");
-  if (nq <= 0 || nk <= 0 || nv <= 0 || nq % head_dim != 0 || nk % head_dim != 0 || nv % 32 != 0)
+  if (head_dim <= 0 || nq <= 0 || nk <= 0 || nv <= 0 || nq % head_dim != 0 || nk % head_dim != 0 || nv % 32 != 0)
     return fail_invalid("linear_rope: q and k widths must be multiples of head_dim, v a multiple of 32");
-  if (seq <= 0 || start_pos < 0 || m % seq != 0) return fail_invalid("linear_rope: m must be a multiple of seq > 0");
-  if (int64_t(start_pos) + seq > table_rows)
-    return fail_invalid("linear_rope: start_pos + seq exceeds the RoPE table length");
+  tk_epilogue e{};
+  e.rope_seq = seq;
+  e.rope_start = start_pos;
+  e.rope_head_dim = head_dim;
+  e.rope_cos = cos_table;
+  e.rope_sin = sin_table;
+  e.rope_table_rows = table_rows;
+  return tk_linear_ex(x, x_row_stride, wq, nq, wk, nk, wv, nv, y, y_row_stride, m, k, &e, dtype, stream);
+}
+
+extern "C" int tk_gate_up_swiglu_ex(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
+                                    void* h, int64_t m, int64_t hidden, int64_t f, const tk_epilogue* epi, int dtype,
+                                    void* stream) {
+  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, hidden)) return rc;
+  if (f <= 0 || f % 8 != 0) return fail_invalid("gate_up_swiglu: f must be a positive multiple of 8");
+  gemm::Extras ex;
+  if (int rc = extras_from(epi, m, hidden, f, 0, false, &ex, "gate_up_swiglu")) return rc;
   if (m == 0) return TK_OK;
-  if (!wq || !wk || !wv) return fail_invalid("linear_rope: NULL weight");
-  if (!cos_table || !sin_table || !aligned16(cos_table) || !aligned16(sin_table))
-    return fail_invalid("linear_rope: RoPE tables must be non-NULL and 16-byte aligned");
-  const int64_t n = nq + nk + nv;
-  if (!y || y_row_stride < n || y_row_stride % 8 != 0) return fail_invalid("linear_rope: bad output or stride");
-  if (n > INT32_MAX || m > INT32_MAX) return fail_invalid("linear_rope: too large");
-  gemm::RopeArgs r;
-  r.cols = static_cast<int>(nq + nk);
-  r.seq = seq;
-  r.start = start_pos;
-  r.half_d = head_dim / 2;
-  r.cos_t = static_cast<const float*>(cos_table);
-  r.sin_t = static_cast<const float*>(sin_table);
+  if (!w_gate || !w_up || !h) return fail_invalid("gate_up_swiglu: NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TK_F16)
-    return gemm::run_linear<TK_F16>(x, x_row_stride, wq, nq, wk, nk, wv, nv, y, y_row_stride, nullptr, m, k, st, r);
-  return gemm::run_linear<TK_BF16>(x, x_row_stride, wq, nq, wk, nk, wv, nv, y, y_row_stride, nullptr, m, k, st, r);
+  if (dtype == TK_F16) return gemm::run_gate_up<TK_F16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st, ex);
+  return gemm::run_gate_up<TK_BF16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st, ex);
 }
 
 extern "C" int tk_gate_up_swiglu(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up, void* h,
                                  int64_t m, int64_t hidden, int64_t f, int dtype, void* stream) {
-  if (int rc = check_gemm_common(dtype, x, x_row_stride, m, hidden)) return rc;
-  if (f <= 0 || f % 8 != 0) return fail_invalid("gate_up_swiglu: f must be a positive multiple of 8");
-  if (m == 0) return TK_OK;
-  if (!w_gate || !w_up || !h) return fail_invalid("gate_up_swiglu: NULL pointer");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TK_F16) return gemm::run_gate_up<TK_F16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
-  return gemm::run_gate_up<TK_BF16>(x, x_row_stride, w_gate, w_up, h, m, hidden, f, st);
+  return tk_gate_up_swiglu_ex(x, x_row_stride, w_gate, w_up, h, m, hidden, f, nullptr, dtype, stream);
 }
 
 extern "C" int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,

@@ -277,8 +277,51 @@ int launch_swiglu(const void* g, int64_t gs, const void* u, int64_t us, void* o,
                        us, o, os, rows, n);
 }
 
+// parts[(c / 32) * m + r] = sum of x[r, c .. c+31]^2: one thread per (row, 32-column chunk),
+// chunks of a row on consecutive threads (the 64-byte loads of a warp are contiguous).
+template <int DT>
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const void* __restrict__ x, int64_t xs, int64_t m,
+                                                         int chunks, float* __restrict__ parts) {
+  pdl_launch_dependents();
+  pdl_wait();  // x is written by an earlier kernel
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= m * chunks) return;
+  const int64_t r = t / chunks;
+  const int c = static_cast<int>(t - r * chunks);
+  using V = Vec<DT>;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + r * xs + c * 32);
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 32 / V::N; ++q) {
+    float f[V::N];
+    V::to_f(src[q], f);
+#pragma unroll
+    for (int i = 0; i < V::N; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  parts[static_cast<int64_t>(c) * m + r] = ss;
+}
+
 }  // namespace
 }  // namespace tk
+
+extern "C" int tk_row_sumsq(const void* x, int64_t x_row_stride, int64_t m, int64_t k, float* parts, int dtype,
+                            void* stream) {
+  using namespace tk;
+  if (!half_dtype(dtype)) return fail_invalid("row_sumsq: dtype must be F16 or BF16");
+  if (m < 0 || k <= 0 || k % 32 != 0 || x_row_stride < k || x_row_stride % 8 != 0)
+    return fail_invalid("row_sumsq: k must be a positive multiple of 32 and the row stride >= k, a multiple of 8");
+  if (m == 0) return TK_OK;
+  if (!x || !parts || !aligned16(x)) return fail_invalid("row_sumsq: NULL or unaligned pointer");
+  const int chunks = static_cast<int>(k / 32);
+  const int64_t threads = m * chunks;
+  const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return launch_kernel(row_sumsq_kernel<TK_F16>, grid, block, 0, st, 1, "row_sumsq_kernel", x, x_row_stride, m,
+                         chunks, parts);
+  return launch_kernel(row_sumsq_kernel<TK_BF16>, grid, block, 0, st, 1, "row_sumsq_kernel", x, x_row_stride, m,
+                       chunks, parts);
+}
 
 extern "C" int tk_rmsnorm(const void* x, int64_t x_row_stride, const void* weight, int w_dtype, void* y,
                           int64_t y_row_stride, int64_t rows, int64_t dim, float eps, int dtype, void* stream) {

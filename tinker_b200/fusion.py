@@ -11,7 +11,21 @@ is replaced by
     h = attn(norm1(x), residual=x)      # o_proj epilogue adds x
     y = ffn(norm2(h), residual=h)       # down_proj epilogue adds h
 
-which is 7 kernels per block and no torch kernel in between. The replacement is
+which is 7 kernels per block and no torch kernel in between. With ``fold_norms`` (the
+default of ``optimize``) the two RMSNorms go into the GEMMs that consume them: their
+weights are multiplied into the q|k|v and gate|up weights (folded copies, made once and
+remade when a source weight changes in place), each consumer epilogue scales its rows by
+1/rms, and the rms statistics come from the producing epilogues (o_proj writes those of
+``h``, down_proj those of the block output, handed to the next block on the output
+tensor; the first block computes them from its input) - 5 kernels per block:
+
+    qkv = linear_rope(x, Wqkv * w1)  * 1/rms(x)        (RoPE epilogue)
+    h   = o_proj(attention(qkv)) + x        -> rms statistics of h
+    g   = swiglu(h (Wg|Wu * w2)) * 1/rms(h)
+    y   = down(g) + h                       -> rms statistics of y
+
+The result differs from norm-then-GEMM only by where the rounding to the model dtype
+happens (the weight product instead of the normalised activations). The replacement is
 bound only after the block's own forward is shown to have exactly that
 dataflow: forward hooks substitute large random tensors for the outputs of the
 four children and record their inputs, and the block must feed ``x`` to norm1,
@@ -28,6 +42,8 @@ import types
 import torch
 import torch.nn as nn
 
+from tinker_b200.kernels.fused_attention import causal_attention
+from tinker_b200.kernels.gemm import gate_up_swiglu, linear, linear_rope, row_sumsq
 from tinker_b200.modules.attention import TinKerAttention
 from tinker_b200.modules.feed_forward import TinKerSwiGLU
 from tinker_b200.modules.normalization import TinKerRMSNorm
@@ -59,6 +75,59 @@ def _fused_forward(self, x: torch.Tensor) -> torch.Tensor:
     return getattr(self, ff)(getattr(self, n2)(h), residual=h)
 
 
+def _fold_sources(block):
+    n1, at, n2, ff = (getattr(block, n) for n in block._tinker_block_parts)
+    return (n1.weight, n2.weight, at.q_proj.weight, at.k_proj.weight, at.v_proj.weight, ff.gate_proj.weight,
+            ff.up_proj.weight)
+
+
+def _folded_weights(block):
+    """The norm weights multiplied into the weights of the GEMMs that consume the norms (made
+    again whenever one of the source tensors was modified in place since)."""
+    src = _fold_sources(block)
+    key = tuple((t.data_ptr(), t._version) for t in src)
+    cached = getattr(block, "_tinker_folded", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    w1, w2, wq, wk, wv, wg, wu = src
+    with torch.no_grad():
+        def fold(w, nw):
+            return (w.float() * nw.float()[None, :]).to(w.dtype).contiguous()
+        folded = (fold(wq, w1), fold(wk, w1), fold(wv, w1), fold(wg, w2), fold(wu, w2))
+    block._tinker_folded = (key, folded)
+    return folded
+
+
+def _can_fold(block, x: torch.Tensor) -> bool:
+    n1, at, n2, ff = (getattr(block, n) for n in block._tinker_block_parts)
+    return (x.dim() == 3 and x.shape[-1] % 32 == 0 and at.cos_table.dtype == torch.float32
+            and at.sin_table.dtype == torch.float32 and at.head_dim % 32 == 0)
+
+
+def _folded_forward(self, x: torch.Tensor) -> torch.Tensor:
+    if not _can_fold(self, x):
+        return _fused_forward(self, x)
+    n1, at, n2, ff = (getattr(self, n) for n in self._tinker_block_parts)
+    wq, wk, wv, wg, wu = _folded_weights(self)
+    B, S, H = x.shape
+    m = B * S
+    ssq_x = getattr(x, "_tinker_row_ssq", None)
+    if ssq_x is None or ssq_x.shape != (H // 32, m) or ssq_x.device != x.device:
+        ssq_x = row_sumsq(x)
+    hq, hkv = at.num_heads * at.head_dim, at.num_kv_heads * at.head_dim
+    qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
+                      row_ssq_eps=n1.eps)
+    a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
+                         at.num_kv_heads, at.head_dim)
+    ssq_h = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
+    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h)
+    g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)
+    ssq_y = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
+    y = linear(g, ff.down_proj.weight, residual=h, row_ssq_out=ssq_y)
+    y._tinker_row_ssq = ssq_y  # the next folded block reads the statistics from here
+    return y
+
+
 def _dataflow_is_prenorm_residual(block: nn.Module, parts, x: torch.Tensor, gen) -> bool:
     """Run the block's own forward with its children's outputs replaced by known
     tensors and check the pre-norm residual dataflow (see the module docstring)."""
@@ -88,8 +157,10 @@ def _dataflow_is_prenorm_residual(block: nn.Module, parts, x: torch.Tensor, gen)
     return True
 
 
-def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: int = 16) -> int:
-    """Give every qualifying pre-norm decoder block the fused forward; returns how many."""
+def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: int = 16,
+                        fold_norms: bool = True) -> int:
+    """Give every qualifying pre-norm decoder block the fused forward (with the RMSNorms folded
+    into the GEMMs when ``fold_norms``); returns how many."""
     fused = 0
     gen = None
     for name, block in model.named_modules():
@@ -116,7 +187,7 @@ def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: i
                 print(f"  [tinker] block {name}: not a pre-norm residual block, not fused")
             continue
         block._tinker_block_parts = parts
-        block.forward = types.MethodType(_fused_forward, block)
+        block.forward = types.MethodType(_folded_forward if fold_norms else _fused_forward, block)
         fused += 1
         if verbose:
             print(f"  [tinker] fused decoder block {name}")

@@ -9,6 +9,8 @@ tinker/modules/feed_forward.py:27-30). Here they are hand-written sm_100a GEMMs:
   optional residual add in the epilogue.
 * ``linear_rope(x, wq, wk, wv, cos, sin, head_dim, start_pos)`` - the q|k|v projection with
   RoPE applied to the q and k columns in the epilogue.
+* ``row_sumsq(x)`` and the ``row_ssq_in`` / ``row_ssq_out`` options: an RMSNorm folded into the
+  GEMM that consumes it (norm weight multiplied into the weights, 1/rms per row in the epilogue).
 * ``gate_up_swiglu(x, w_gate, w_up)`` - ``silu(x @ w_gate.T) * (x @ w_up.T)`` as one
   GEMM with the SwiGLU applied to the fp32 accumulators.
 * ``swiglu_ffn(x, w_gate, w_up, w_down, residual=None)`` - the whole FFN.
@@ -39,9 +41,60 @@ def _check_x(x: torch.Tensor) -> torch.Tensor:
     return x2
 
 
+def _epilogue(residual=None, row_ssq_in=None, row_ssq_eps=1e-6, row_ssq_out=None, rope=None):
+    """A ``tk_epilogue`` for the ``_ex`` entry points (None when only the plain store is needed)."""
+    if residual is None and row_ssq_in is None and row_ssq_out is None and rope is None:
+        return None
+    e = _lib.Epilogue()
+    e.residual = None if residual is None else residual.data_ptr()
+    if row_ssq_in is not None:
+        if row_ssq_in.dtype != torch.float32 or row_ssq_in.dim() != 2 or not row_ssq_in.is_contiguous():
+            raise ValueError("row_ssq_in must be a contiguous float32 [parts, m] tensor")
+        e.row_ssq_in = row_ssq_in.data_ptr()
+        e.row_ssq_parts = row_ssq_in.shape[0]
+        e.row_ssq_eps = float(row_ssq_eps)
+    if row_ssq_out is not None:
+        e.row_ssq_out = row_ssq_out.data_ptr()
+    if rope is not None:
+        cos, sin, head_dim, seq, start_pos = rope
+        e.rope_cos, e.rope_sin = cos.data_ptr(), sin.data_ptr()
+        e.rope_head_dim, e.rope_seq, e.rope_start = head_dim, seq, int(start_pos)
+        e.rope_table_rows = cos.shape[0]
+    return e
+
+
+def _check_ssq(t: torch.Tensor | None, m: int, parts: int | None, what: str):
+    if t is None:
+        return
+    if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != m or not t.is_contiguous():
+        raise ValueError(f"{what} must be a contiguous float32 [parts, {m}] tensor")
+    if parts is not None and t.shape[0] != parts:
+        raise ValueError(f"{what} must have {parts} partial sums per row")
+
+
+def row_sumsq(x: torch.Tensor) -> torch.Tensor:
+    """Per-32-column partial sums of squares of the rows of ``x`` [..., k]: float32 [k/32, rows],
+    the ``row_ssq_in`` of a GEMM that consumes ``rmsnorm(x)`` with the norm weight folded in."""
+    dev = _lib.require_cuda(x)
+    x2 = _check_x(x)
+    m, k = x2.shape
+    parts = torch.empty((k + 31) // 32, m, dtype=torch.float32, device=x.device)
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_row_sumsq(x2.data_ptr(), row_stride(x2), m, k, parts.data_ptr(),
+                                           _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_row_sumsq", 1)
+    return parts
+
+
 def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2: torch.Tensor | None = None,
-           residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``x @ cat([w0, w1, w2]).T (+ residual)``; x [..., k], w* [n*, k]."""
+           residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+           row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,
+           row_ssq_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ cat([w0, w1, w2]).T (+ residual)``; x [..., k], w* [n*, k].
+
+    ``row_ssq_in`` ([parts, m] float32, from ``row_sumsq`` or another GEMM's ``row_ssq_out``) scales
+    each output row by ``1/sqrt(mean(x_row^2) + row_ssq_eps)``: with an RMSNorm weight folded into
+    the weights this is ``rmsnorm(x) @ W.T``. ``row_ssq_out`` ([ceil(n/32), m] float32) receives the
+    partial sums of squares of the stored rows for the next folded RMSNorm."""
     ws = [w for w in (w0, w1, w2) if w is not None]
     dev = _lib.require_cuda(x, *ws)
     x2 = _check_x(x)
@@ -59,20 +112,30 @@ def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2
         r = residual.reshape(m, n)
         if not r.is_contiguous() or r.dtype != x.dtype:
             r = r.contiguous().to(x.dtype)
+    _check_ssq(row_ssq_in, m, None, "row_ssq_in")
+    _check_ssq(row_ssq_out, m, (n + 31) // 32, "row_ssq_out")
     ptrs = [w.data_ptr() for w in ws] + [None] * (3 - len(ws))
     rows = [w.shape[0] for w in ws] + [0] * (3 - len(ws))
+    e = _epilogue(r, row_ssq_in, row_ssq_eps, row_ssq_out)
     with call_ctx(dev):
-        _lib.check(_lib.lib().tk_linear(x2.data_ptr(), row_stride(x2), ptrs[0], rows[0], ptrs[1], rows[1], ptrs[2],
-                                        rows[2], out.data_ptr(), n, None if r is None else r.data_ptr(), m, k,
-                                        _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear", 1)
+        if e is None:
+            _lib.check(_lib.lib().tk_linear(x2.data_ptr(), row_stride(x2), ptrs[0], rows[0], ptrs[1], rows[1], ptrs[2],
+                                            rows[2], out.data_ptr(), n, None, m, k,
+                                            _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear", 1)
+        else:
+            _lib.check(_lib.lib().tk_linear_ex(x2.data_ptr(), row_stride(x2), ptrs[0], rows[0], ptrs[1], rows[1],
+                                               ptrs[2], rows[2], out.data_ptr(), n, m, k, e,
+                                               _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear_ex", 1)
     return out.reshape(*lead, n)
 
 
 def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, cos_table: torch.Tensor,
-                sin_table: torch.Tensor, head_dim: int, start_pos: int = 0) -> torch.Tensor:
+                sin_table: torch.Tensor, head_dim: int, start_pos: int = 0,
+                row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
     """``x @ cat([wq, wk, wv]).T`` for x [batch, seq, hidden] with RoPE applied to the q and k
     columns in the GEMM epilogue (each value rounded to the output dtype, then rotated in fp32 at
-    position ``start_pos + s``): the q|k|v projection plus the RoPE of ``fused_attention``."""
+    position ``start_pos + s``): the q|k|v projection plus the RoPE of ``fused_attention``.
+    ``row_ssq_in`` / ``row_ssq_eps`` as in ``linear`` (the attention RMSNorm folded in)."""
     dev = _lib.require_cuda(x, wq, wk, wv, cos_table, sin_table)
     if x.dim() != 3:
         raise ValueError("linear_rope: x must be [batch, seq, hidden]")
@@ -86,17 +149,29 @@ def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.T
         raise ValueError(f"RoPE tables must be [max_seq_len, {head_dim // 2}], got {tuple(c.shape)}")
     n = wq.shape[0] + wk.shape[0] + wv.shape[0]
     m = x2.shape[0]
+    _check_ssq(row_ssq_in, m, None, "row_ssq_in")
     out = torch.empty(m, n, dtype=x.dtype, device=x.device)
     with call_ctx(dev):
-        _lib.check(_lib.lib().tk_linear_rope(
-            x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0], wv.data_ptr(),
-            wv.shape[0], out.data_ptr(), n, m, k, S, int(start_pos), head_dim, c.data_ptr(), s_.data_ptr(),
-            c.shape[0], _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear_rope", 1)
+        if row_ssq_in is None:
+            _lib.check(_lib.lib().tk_linear_rope(
+                x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0],
+                wv.data_ptr(), wv.shape[0], out.data_ptr(), n, m, k, S, int(start_pos), head_dim, c.data_ptr(),
+                s_.data_ptr(), c.shape[0], _lib.dtype_code(x.dtype), _lib.stream_ptr(dev)), "tk_linear_rope", 1)
+        else:
+            if wq.shape[0] % head_dim or wk.shape[0] % head_dim:
+                raise ValueError("linear_rope: q and k widths must be multiples of head_dim")
+            e = _epilogue(None, row_ssq_in, row_ssq_eps, None, (c, s_, head_dim, S, start_pos))
+            _lib.check(_lib.lib().tk_linear_ex(
+                x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0],
+                wv.data_ptr(), wv.shape[0], out.data_ptr(), n, m, k, e, _lib.dtype_code(x.dtype),
+                _lib.stream_ptr(dev)), "tk_linear_ex", 1)
     return out.reshape(B, S, n)
 
 
-def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
-    """``silu(x @ w_gate.T) * (x @ w_up.T)`` as one GEMM with a SwiGLU epilogue."""
+def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                   row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
+    """``silu(x @ w_gate.T) * (x @ w_up.T)`` as one GEMM with a SwiGLU epilogue; ``row_ssq_in`` /
+    ``row_ssq_eps`` as in ``linear`` (the FFN RMSNorm folded into both weights)."""
     dev = _lib.require_cuda(x, w_gate, w_up)
     x2 = _check_x(x)
     k = x2.shape[1]
@@ -104,11 +179,19 @@ def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor) ->
     if wg.shape != wu.shape:
         raise ValueError("gate and up weights must have the same shape")
     f = wg.shape[0]
-    h = torch.empty(x2.shape[0], f, dtype=x.dtype, device=x.device)
+    m = x2.shape[0]
+    _check_ssq(row_ssq_in, m, None, "row_ssq_in")
+    h = torch.empty(m, f, dtype=x.dtype, device=x.device)
+    e = _epilogue(None, row_ssq_in, row_ssq_eps)
     with call_ctx(dev):
-        _lib.check(_lib.lib().tk_gate_up_swiglu(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
-                                                h.data_ptr(), x2.shape[0], k, f, _lib.dtype_code(x.dtype),
-                                                _lib.stream_ptr(dev)), "tk_gate_up_swiglu", 1)
+        if e is None:
+            _lib.check(_lib.lib().tk_gate_up_swiglu(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
+                                                    h.data_ptr(), m, k, f, _lib.dtype_code(x.dtype),
+                                                    _lib.stream_ptr(dev)), "tk_gate_up_swiglu", 1)
+        else:
+            _lib.check(_lib.lib().tk_gate_up_swiglu_ex(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
+                                                       h.data_ptr(), m, k, f, e, _lib.dtype_code(x.dtype),
+                                                       _lib.stream_ptr(dev)), "tk_gate_up_swiglu_ex", 1)
     return h.reshape(*x.shape[:-1], f)
 
 

@@ -40,15 +40,17 @@ def optimize(
     verbose: bool = False,
     graph_clone_output: bool = True,
     fuse_blocks: bool = True,
+    fold_norms: bool = True,
 ) -> nn.Module:
     """optimize a model for inference on a B200.
 
-    Same arguments as the reference, plus two:
+    Same arguments as the reference, plus three:
     ``graph_clone_output`` (default True, as in the reference) controls whether the
     CUDA-graph wrapper returns a clone of its static output or the static output
     itself; ``fuse_blocks`` (default True) gives qualifying pre-norm decoder blocks
     a forward whose residual adds run inside the GEMM epilogues
-    (``tinker_b200.fusion``), after checking the block's dataflow.
+    (``tinker_b200.fusion``), after checking the block's dataflow; ``fold_norms``
+    (default True) also folds those blocks' RMSNorms into the GEMMs after them.
     """
     model.eval()
     params = list(model.parameters())
@@ -78,7 +80,7 @@ def optimize(
         share_rope_tables(model)
 
     if fuse_blocks and replace_attention and replace_ffn and replace_norm:
-        n = fuse_decoder_blocks(model, verbose=verbose)
+        n = fuse_decoder_blocks(model, verbose=verbose, fold_norms=fold_norms)
         if verbose:
             print(f"  [tinker] fused {n} decoder blocks (residual adds in the GEMM epilogues)")
 
