@@ -54,6 +54,9 @@ def _args():
                     help="profiling helper: time only the graph replay or one kernel kind (268M shapes), or "
                          "the Qwen-shaped batched forward (--qwen-batch sequences of 512)")
     ap.add_argument("--qwen-batch", type=int, default=64)
+    ap.add_argument("--sweep", default=None, metavar="KINDS",
+                    help="run the standalone sweeps instead (comma list of rmsnorm, ffn, attention, model1b; "
+                         "tinker_b200.sweep), one JSON line per case")
     return ap.parse_args()
 
 
@@ -546,7 +549,10 @@ def run_ours(args):
 
 def main():
     args = _args()
-    if args.impl == "reference":
+    if args.sweep:
+        from tinker_b200 import sweep
+        sweep.main(["--only", args.sweep])
+    elif args.impl == "reference":
         run_reference(args)
     elif args.only:
         run_only(args)

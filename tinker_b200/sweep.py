@@ -1,0 +1,253 @@
+"""Standalone kernel sweeps and the ~1B decoder, each against the reference's eager torch path
+on the same GPU.
+
+    python -m tinker_b200.sweep [--only rmsnorm,ffn,attention,model1b] [--dtypes fp16,bf16]
+
+One JSON line per case on stdout. The cases are the standalone configurations the reference
+benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of
+the measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096}; the SwiGLU
+FFN (gate|up GEMM with the SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at
+1024 -> 2816 and 2048 -> 5632; causal RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512,
+2048} x head_dim {64, 128} x heads 16/4, 16/16, 16/1; and the ~1B Llama-style decoder at batch
+{1, 16} x seq {128, 2048}. The comparison arm restates the reference's eager fallbacks in torch
+(`_rmsnorm_pytorch` tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
+tinker/modules/feed_forward.py:26-30 with `_swiglu_pytorch` fused_swiglu.py:57-58,
+`_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA.
+
+Timing: each call is captured 20+ times in a CUDA graph, rotating over enough copies of its
+inputs that one replay touches more than twice the 126 MB L2 (so HBM figures are not L2 hits),
+and the graph is replayed after warm-up; CUDA events around the replays give time per call.
+Roofline denominators come from MEASURED_PEAKS.json (HBM copy GB/s, bf16 dense TF/s, burst).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+L2_BYTES = 126 * 1024 * 1024
+DTYPES = {"fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "tflops": float(d["bf16_tflops"]), "note": "of measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "note": "of fallback"}
+
+
+def _copies(bytes_per_call: int) -> int:
+    """How many input copies one graph replay must rotate over to exceed twice the L2."""
+    return max(1, min(64, math.ceil(2 * L2_BYTES / max(1, bytes_per_call))))
+
+
+def _time_graph(fns, min_calls: int = 20) -> float:
+    """Microseconds per call of the closures in ``fns`` (rotated), inside one CUDA graph."""
+    calls = max(min_calls, len(fns))
+    for fn in fns[:2]:
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(calls):
+            fns[i % len(fns)]()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * calls)
+
+
+# ---------------------------------------------------------------- reference eager arms (torch)
+
+def _ref_rmsnorm(x, w, eps):
+    xf = x.float()
+    return (xf * xf.pow(2).mean(-1, keepdim=True).add(eps).rsqrt() * w.float()).to(x.dtype)
+
+
+def _ref_ffn(x, wg, wu, wd):
+    return F.linear(F.silu(F.linear(x, wg)).mul_(F.linear(x, wu)), wd)
+
+
+def _ref_rope(x, cos, sin):  # x [B, H, S, D]
+    S = x.shape[2]
+    c, s = cos[:S][None, None], sin[:S][None, None]
+    xe, xo = x[..., 0::2].float(), x[..., 1::2].float()
+    return torch.stack([xe * c - xo * s, xe * s + xo * c], dim=-1).flatten(-2).to(x.dtype)
+
+
+def _ref_attention(q, k, v, cos, sin, hq, hkv, d):
+    B, S, _ = q.shape
+    q = _ref_rope(q.view(B, S, hq, d).transpose(1, 2), cos, sin)
+    k = _ref_rope(k.view(B, S, hkv, d).transpose(1, 2), cos, sin)
+    v = v.view(B, S, hkv, d).transpose(1, 2)
+    if hq != hkv:
+        k = k.unsqueeze(2).expand(-1, -1, hq // hkv, -1, -1).reshape(B, hq, S, d)
+        v = v.unsqueeze(2).expand(-1, -1, hq // hkv, -1, -1).reshape(B, hq, S, d)
+    out = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    return out.transpose(1, 2).contiguous().view(B, S, hq * d)
+
+
+# ---------------------------------------------------------------- sweeps
+
+def sweep_rmsnorm(dtypes, peaks, emit):
+    from tinker_b200.kernels import fused_rmsnorm
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for dt in dtypes:
+        for rows in (128, 4096, 65536):
+            for h in (1024, 2048, 4096):
+                nbytes = rows * h * 4 + 2 * h
+                n = _copies(nbytes)
+                xs = [torch.randn(rows, h, device="cuda", generator=g).to(dt) for _ in range(n)]
+                w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+                ours = _time_graph([lambda x=x: fused_rmsnorm(x, w, 1e-6) for x in xs])
+                ref = _time_graph([lambda x=x: _ref_rmsnorm(x, w, 1e-6) for x in xs])
+                gbs = nbytes / ours * 1e-3
+                emit({"kind": "rmsnorm", "case": f"rows {rows} x hidden {h}", "dtype": str(dt)[6:],
+                      "ours_us": round(ours, 2), "ref_eager_us": round(ref, 2), "speedup": round(ref / ours, 2),
+                      "bound": "hbm", "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
+                      "peak": f"{peaks['hbm_gbs']} GB/s {peaks['note']}", "bytes": nbytes})
+                del xs
+
+
+def sweep_ffn(dtypes, peaks, emit):
+    from tinker_b200.kernels import swiglu_ffn
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for dt in dtypes:
+        for h, f in ((1024, 2816), (2048, 5632)):
+            wg = (0.02 * torch.randn(f, h, device="cuda", generator=g)).to(dt)
+            wu = (0.02 * torch.randn(f, h, device="cuda", generator=g)).to(dt)
+            wd = (0.02 * torch.randn(h, f, device="cuda", generator=g)).to(dt)
+            for t in (128, 4096, 16384):
+                flops = 6 * t * h * f
+                nbytes = 2 * (3 * h * f + 2 * t * h) + 2 * 2 * t * f
+                n = _copies(2 * t * h) if t <= 4096 else 1
+                xs = [torch.randn(t, h, device="cuda", generator=g).to(dt) for _ in range(n)]
+                ours = _time_graph([lambda x=x: swiglu_ffn(x, wg, wu, wd) for x in xs])
+                ref = _time_graph([lambda x=x: _ref_ffn(x, wg, wu, wd) for x in xs])
+                tf = flops / ours * 1e-6
+                gbs = nbytes / ours * 1e-3
+                bound = "hbm" if t <= 128 else "tensor"
+                frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["tflops"]
+                emit({"kind": "swiglu_ffn", "case": f"tokens {t}, {h} -> {f}", "dtype": str(dt)[6:],
+                      "ours_us": round(ours, 2), "ref_eager_us": round(ref, 2), "speedup": round(ref / ours, 2),
+                      "bound": bound, "tflops": round(tf, 1), "gbs": round(gbs, 1), "frac": round(frac, 3),
+                      "peak": (f"{peaks['hbm_gbs']} GB/s" if bound == "hbm" else f"{peaks['tflops']} TF/s")
+                      + f" {peaks['note']}", "flops": flops, "bytes": nbytes})
+                del xs
+
+
+def sweep_attention(dtypes, peaks, emit):
+    from tinker_b200.kernels import causal_attention, fused_attention, precompute_rope_tables
+    g = torch.Generator(device="cuda").manual_seed(2)
+    for dt in dtypes:
+        for d in (64, 128):
+            cos, sin = precompute_rope_tables(d, 2048, 10000.0, device="cuda")
+            for b in (1, 8, 32):
+                for s in (128, 512, 2048):
+                    for hq, hkv in ((16, 4), (16, 16), (16, 1)):
+                        flops = 2 * 2 * b * hq * d * s * s // 2  # causal convention: half of the dense S x S
+                        nbytes = 2 * b * s * d * (2 * hq + 2 * hkv)
+                        n = _copies(nbytes)
+                        qkv = [(torch.randn(b, s, hq * d, device="cuda", generator=g).to(dt),
+                                torch.randn(b, s, hkv * d, device="cuda", generator=g).to(dt),
+                                torch.randn(b, s, hkv * d, device="cuda", generator=g).to(dt)) for _ in range(n)]
+                        rope = _time_graph([lambda t=t: fused_attention(*t, cos, sin, hq, hkv, d) for t in qkv])
+                        plain = _time_graph([lambda t=t: causal_attention(*t, hq, hkv, d) for t in qkv])
+                        ref = _time_graph([lambda t=t: _ref_attention(*t, cos, sin, hq, hkv, d) for t in qkv])
+                        tf_rope, tf_plain = flops / rope * 1e-6, flops / plain * 1e-6
+                        emit({"kind": "attention", "case": f"B {b} S {s} D {d} heads {hq}/{hkv}",
+                              "dtype": str(dt)[6:], "ours_rope_us": round(rope, 2), "ours_prerotated_us": round(plain, 2),
+                              "ref_eager_us": round(ref, 2), "speedup": round(ref / rope, 2),
+                              "bound": "latency" if s <= 128 else "tensor", "tflops_rope": round(tf_rope, 1),
+                              "tflops_prerotated": round(tf_plain, 1), "frac_rope": round(tf_rope / peaks["tflops"], 3),
+                              "frac_prerotated": round(tf_plain / peaks["tflops"], 3),
+                              "peak": f"{peaks['tflops']} TF/s {peaks['note']}", "flops": flops, "bytes": nbytes})
+                        del qkv
+
+
+def _time_replays(graph, reps: int) -> float:
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def sweep_model1b(peaks, emit):
+    import tinker_b200
+    from tinker_b200.eager_model import LLAMA_1B, build_model, make_tokens
+    cfg = LLAMA_1B
+    ref_model = build_model(cfg, seed=0).to("cuda", torch.float16).eval()
+    params = sum(p.numel() for p in ref_model.parameters())
+    for b, s in ((1, 128), (16, 2048)):
+        reps = 20 if b * s <= 128 else 3
+        tok = make_tokens(cfg, b, s, seed=1).cuda()
+        with torch.inference_mode():
+            ref = _time_graph([lambda: ref_model(tok)], min_calls=reps)
+        torch.cuda.empty_cache()
+        m = tinker_b200.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, cuda_graph=True,
+                                 graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size, graph_clone_output=False)
+        m._static_input.copy_(tok)
+        ours = _time_replays(m._graph, reps)
+        flops = 2 * b * s * (params - cfg.vocab_size * cfg.hidden_size)  # embedding rows are a gather
+        flops += 2 * 2 * b * cfg.num_layers * cfg.num_heads * cfg.head_dim * s * s // 2
+        wbytes = 2 * (params - cfg.vocab_size * cfg.hidden_size)
+        bound = "hbm" if b * s <= 128 else "tensor"
+        tf = flops / ours * 1e-6
+        gbs = (wbytes + 2 * b * s * cfg.vocab_size) / ours * 1e-3
+        emit({"kind": "model_1b", "case": f"batch {b} x seq {s}", "dtype": "float16", "params": params,
+              "ours_us": round(ours, 1), "ref_eager_us": round(ref, 1), "speedup": round(ref / ours, 2),
+              "tokens_per_s": round(b * s / ours * 1e6), "bound": bound, "tflops": round(tf, 1), "gbs": round(gbs, 1),
+              "frac": round(gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["tflops"], 3),
+              "note": "reference arm: the unpatched fp16 model (cuBLAS + SDPA) captured in a CUDA graph"})
+        del m
+        torch.cuda.empty_cache()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="rmsnorm,ffn,attention,model1b")
+    ap.add_argument("--dtypes", default="fp16,bf16")
+    args = ap.parse_args(argv)
+    torch.cuda.set_device(0)
+    peaks = _peaks()
+    dtypes = [DTYPES[d] for d in args.dtypes.split(",")]
+
+    def emit(d):
+        print(json.dumps(d), flush=True)
+
+    kinds = args.only.split(",")
+    with torch.inference_mode():
+        if "rmsnorm" in kinds:
+            sweep_rmsnorm(dtypes, peaks, emit)
+        if "ffn" in kinds:
+            sweep_ffn(dtypes, peaks, emit)
+        if "attention" in kinds:
+            sweep_attention(dtypes, peaks, emit)
+    if "model1b" in kinds:
+        sweep_model1b(peaks, emit)
+
+
+if __name__ == "__main__":
+    main()
