@@ -112,6 +112,20 @@ TK_API int tk_rope_attention(const void* q, int64_t q_tok_stride, const void* k,
                       int num_kv_heads, int head_dim, int start_pos, int dtype, void* stream);
 
 /*
+ * RoPE of q and k in one pass: out[b, s, :] = [rope(q heads) | rope(k heads)], each interleaved
+ * pair rotated in fp32 at position start_pos + s and rounded to dtype, exactly as
+ * tk_rope_attention rotates on load (the reference's _rope_kernel,
+ * tinker/kernels/fused_attention.py:19-69, on its permuted copies :199-214). Feeds
+ * tk_causal_attention for long sequences, where rotating on load would re-read the cos/sin
+ * rows of every key tile in every CTA. out: token stride >= (num_heads + num_kv_heads) *
+ * head_dim; head_dim a multiple of 8; all strides multiples of 8 elements.
+ */
+TK_API int tk_rope_qk(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride, const void* cos_table,
+               const void* sin_table, int table_dtype, int64_t table_rows, void* out, int64_t out_tok_stride,
+               int batch, int seq, int num_heads, int num_kv_heads, int head_dim, int start_pos, int dtype,
+               void* stream);
+
+/*
  * The same causal GQA attention on q and k that already carry RoPE (the q|k|v
  * projection applied it in its epilogue, tk_linear_rope): the kernel of
  * tk_rope_attention without the rotation. Together with tk_linear_rope it

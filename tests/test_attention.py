@@ -267,3 +267,81 @@ def test_linear_rope_rejects_bad_arguments():
         linear_rope(x, w, w, w, cos, sin, 64, start_pos=1)
     with pytest.raises(TypeError, match="float32"):
         linear_rope(x, w, w, w, cos.half(), sin.half(), 64)
+
+
+def _rope_attention_direct(q, k, v, cos, sin, hq, hkv, d, start_pos=0):
+    """tk_rope_attention itself (RoPE on load), whatever fused_attention picks for this length."""
+    from tinker_b200 import _lib
+    B, S, _ = q.shape
+    out = torch.empty(B, S, hq * d, dtype=q.dtype, device=q.device)
+    _lib.check(_lib.lib().tk_rope_attention(
+        q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), v.data_ptr(), v.stride(1), cos.data_ptr(),
+        sin.data_ptr(), _lib.dtype_code(cos.dtype), cos.shape[0], out.data_ptr(), hq * d, B, S, hq, hkv, d,
+        start_pos, _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device)), "tk_rope_attention", 1)
+    return out
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B, S, hq, hkv, d, start_pos", [(2, 1000, 16, 4, 64, 3), (1, 2048, 8, 8, 128, 0),
+                                                          (3, 384, 14, 2, 64, 0)])
+def test_rope_on_load_kernel_long_sequences(dt, B, S, hq, hkv, d, start_pos):
+    """The RoPE-on-load kernel at lengths where fused_attention uses the separate RoPE pass."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import precompute_rope_tables
+    dtype = DTYPES[dt]
+    g = torch.Generator(device="cuda").manual_seed(S + d)
+    q = torch.randn(B, S, hq * d, device="cuda", generator=g).to(dtype)
+    k = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(dtype)
+    v = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(dtype)
+    cos, sin = precompute_rope_tables(d, S + start_pos, device="cuda")
+    out = _rope_attention_direct(q, k, v, cos, sin, hq, hkv, d, start_pos)
+    ref = oracle.attention(np32(q), np32(k), np32(v), np32(cos), np32(sin), hq, hkv, d, start_pos,
+                           io_dtype=NP_NAME[dtype])
+    assert rel_err(np32(out), ref) <= TOL
+
+
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_rope_qk_pass_matches_oracle_rope(dt, table_dtype):
+    """tk_rope_qk = the reference's RoPE (fused_attention.py:165-173 arithmetic) on q and k heads."""
+    require_b200()
+    from tinker_b200 import _lib
+    from tinker_b200.kernels.fused_attention import precompute_rope_tables
+    dtype = DTYPES[dt]
+    B, S, hq, hkv, d, start = 2, 300, 8, 2, 64, 7
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, S, (hq + 2 * hkv) * d, device="cuda", generator=g).to(dtype)
+    q, k = qkv[..., :hq * d], qkv[..., hq * d:(hq + hkv) * d]
+    cos, sin = precompute_rope_tables(d, S + start, device="cuda", dtype=table_dtype)
+    out = torch.empty(B, S, (hq + hkv) * d, dtype=dtype, device="cuda")
+    _lib.check(_lib.lib().tk_rope_qk(q.data_ptr(), qkv.stride(1), k.data_ptr(), qkv.stride(1), cos.data_ptr(),
+                                     sin.data_ptr(), _lib.dtype_code(table_dtype), cos.shape[0], out.data_ptr(),
+                                     (hq + hkv) * d, B, S, hq, hkv, d, start, _lib.dtype_code(dtype),
+                                     _lib.stream_ptr(qkv.device)), "tk_rope_qk", 1)
+    for heads, src, lo in ((hq, q, 0), (hkv, k, hq * d)):
+        x = np32(src).reshape(B, S, heads, d).transpose(0, 2, 1, 3)
+        ref = oracle.apply_rope(x, np32(cos), np32(sin), start, out_dtype=NP_NAME[dtype])
+        got = np32(out[..., lo:lo + heads * d]).reshape(B, S, heads, d).transpose(0, 2, 1, 3)
+        # same fp32 arithmetic, one rounding: equal up to one ulp where an FMA contraction differs
+        np.testing.assert_allclose(got, ref, rtol=2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10, atol=1e-6)
+
+
+@pytest.mark.parametrize("entry", ["causal", "rope"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_repeated_calls_are_bitwise_identical(entry, d):
+    """Every tile waits for the operands it reads: repeated calls on the same inputs give the same
+    bits (a tile computed from smem that TMA had not yet filled shows up as run-to-run noise)."""
+    require_b200()
+    from tinker_b200.kernels.fused_attention import causal_attention, precompute_rope_tables
+    B, S, hq, hkv = 4, 1024, 16, 4
+    g = torch.Generator(device="cuda").manual_seed(d)
+    q = torch.randn(B, S, hq * d, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(torch.bfloat16)
+    cos, sin = precompute_rope_tables(d, S, device="cuda")
+    if entry == "causal":
+        outs = [causal_attention(q, k, v, hq, hkv, d) for _ in range(8)]
+    else:
+        outs = [_rope_attention_direct(q, k, v, cos, sin, hq, hkv, d) for _ in range(8)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])

@@ -44,6 +44,7 @@ SIGNATURES = {
     "tk_add_rmsnorm": [_P, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _P],
     "tk_swiglu": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P],
     "tk_rope_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _I, _P],
+    "tk_rope_qk": [_P, _I64, _P, _I64, _P, _P, _I, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _I, _P],
     "tk_causal_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _I, _I, _I, _P],
     "tk_linear": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _P],
     "tk_linear_rope": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I,

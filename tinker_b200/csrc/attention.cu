@@ -259,7 +259,9 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       const uint32_t t_sa = tmem_base, t_sb = tmem_base + 128;
       const uint32_t t_oa = tmem_base + 256, t_ob = tmem_base + 256 + D;
 
-      bool ok = mbar_wait(bars + B_Q_READY, 0) && wait_k(0);
+      // with RoPE the softmax warps publish the rotated Q tiles (Q_READY after they saw Q_FULL);
+      // without it nobody touches Q, so wait for the TMA transaction itself
+      bool ok = mbar_wait(bars + (ROPE ? B_Q_READY : B_Q_FULL), 0) && wait_k(0);
       if (ok) {
         tc_fence_after();
         issue_s(q_a, slot_addr(0), t_sa);
@@ -492,6 +494,39 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
                        ROPE ? "rope_attention_kernel" : "causal_attention_kernel", tq, tk_, tv, p);
 }
 
+// RoPE of q and k in one pass, into out [batch, seq, (num_heads + num_kv_heads) * D] (q heads,
+// then k heads): one thread per 8 consecutive elements (4 interleaved pairs) of a token row.
+template <int DT>
+__global__ void __launch_bounds__(256) rope_qk_kernel(const void* __restrict__ q, int64_t qs,
+                                                       const void* __restrict__ k, int64_t ks, void* __restrict__ out,
+                                                       int64_t os, Params p, int head_dim, int64_t tokens) {
+  using Dx = Dt<DT>;
+  pdl_launch_dependents();
+  pdl_wait();  // q and k are written by the previous kernel
+  const int qcols = p.num_heads * head_dim;
+  const int vecs = (qcols + p.num_kv_heads * head_dim) / 8;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= tokens * vecs) return;
+  const int64_t tok = t / vecs;
+  const int col = static_cast<int>(t - tok * vecs) * 8;
+  const int64_t pos = static_cast<int64_t>(p.start_pos) + tok % p.seq;
+  const uint16_t* src = col < qcols ? reinterpret_cast<const uint16_t*>(q) + tok * qs + col
+                                    : reinterpret_cast<const uint16_t*>(k) + tok * ks + (col - qcols);
+  const int i0 = (col % head_dim) / 2;
+  float c[4], sn[4];
+  load_cs4(p.cos_t, p.table_dtype, pos * (head_dim / 2) + i0, c);
+  load_cs4(p.sin_t, p.table_dtype, pos * (head_dim / 2) + i0, sn);
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = Dx::unpack(*reinterpret_cast<typename Dx::T2*>(&w[i]));
+    typename Dx::T2 o = Dx::pack(x.x * c[i] - x.y * sn[i], x.x * sn[i] + x.y * c[i]);
+    w[i] = *reinterpret_cast<uint32_t*>(&o);
+  }
+  *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + tok * os + col) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <bool ROPE>
 int dispatch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, int64_t vs, const Params& p,
              int dtype, int head_dim, cudaStream_t st) {
@@ -581,4 +616,46 @@ extern "C" int tk_causal_attention(const void* q, int64_t q_tok_stride, const vo
   if (empty) return TK_OK;
   return attn::dispatch<false>(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, p, dtype, head_dim,
                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tk_rope_qk(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                          const void* cos_table, const void* sin_table, int table_dtype, int64_t table_rows,
+                          void* out, int64_t out_tok_stride, int batch, int seq, int num_heads, int num_kv_heads,
+                          int head_dim, int start_pos, int dtype, void* stream) {
+  using namespace tk;
+  if (!half_dtype(dtype)) return fail_invalid("rope_qk: dtype must be F16 or BF16");
+  if (!valid_dtype(table_dtype)) return fail_invalid("rope_qk: table dtype must be F16, BF16 or F32");
+  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || start_pos < 0 || head_dim <= 0 ||
+      head_dim % 8 != 0)
+    return fail_invalid("rope_qk: invalid sizes (head_dim must be a positive multiple of 8)");
+  const int64_t width = int64_t(num_heads + num_kv_heads) * head_dim;
+  if (q_tok_stride < int64_t(num_heads) * head_dim || k_tok_stride < int64_t(num_kv_heads) * head_dim ||
+      out_tok_stride < width)
+    return fail_invalid("rope_qk: token stride smaller than heads * head_dim");
+  if (q_tok_stride % 8 || k_tok_stride % 8 || out_tok_stride % 8)
+    return fail_invalid("rope_qk: token strides must be multiples of 8 elements");
+  if (int64_t(start_pos) + seq > table_rows)
+    return fail_invalid("rope_qk: start_pos + seq exceeds the RoPE table length");
+  if (batch == 0 || seq == 0) return TK_OK;
+  if (!q || !k || !cos_table || !sin_table || !out) return fail_invalid("rope_qk: NULL pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(out) || !aligned16(cos_table) || !aligned16(sin_table))
+    return fail_invalid("rope_qk: q, k, out and the RoPE tables must be 16-byte aligned");
+  attn::Params p{};
+  p.seq = seq;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.start_pos = start_pos;
+  p.table_rows = table_rows;
+  p.cos_t = cos_table;
+  p.sin_t = sin_table;
+  p.table_dtype = table_dtype;
+  const int64_t tokens = int64_t(batch) * seq;
+  const int64_t threads = tokens * (width / 8);
+  const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return launch_kernel(attn::rope_qk_kernel<TK_F16>, grid, block, 0, st, 1, "rope_qk_kernel", q, q_tok_stride, k,
+                         k_tok_stride, out, out_tok_stride, p, head_dim, tokens);
+  return launch_kernel(attn::rope_qk_kernel<TK_BF16>, grid, block, 0, st, 1, "rope_qk_kernel", q, q_tok_stride, k,
+                       k_tok_stride, out, out_tok_stride, p, head_dim, tokens);
 }

@@ -6,7 +6,9 @@ the same torch arithmetic, and ``fused_attention`` (:234-238) with the same
 arguments and result. Instead of the reference's three permute copies, two
 in-place RoPE launches and the attention launch (:195-231), one tcgen05 kernel
 reads q/k/v in their ``[batch, seq, heads * head_dim]`` projection layout,
-applies RoPE on load and writes the output in that layout.
+applies RoPE on load and writes the output in that layout; from
+``ROPE_PREPASS_MIN_SEQ`` on, one pass rotates q and k (``tk_rope_qk``) and the
+attention kernel runs without RoPE.
 """
 
 from __future__ import annotations
@@ -15,6 +17,11 @@ import torch
 
 from tinker_b200 import _lib
 from tinker_b200.kernels._common import call_ctx
+
+
+# From this sequence length on, fused_attention rotates q and k in a separate pass (tk_rope_qk)
+# and runs the attention kernel without RoPE; below it, one kernel rotates on load.
+ROPE_PREPASS_MIN_SEQ = 256
 
 
 def precompute_rope_tables(head_dim, max_seq_len, theta=10000.0, device=None, dtype=torch.float32):
@@ -62,6 +69,21 @@ def fused_attention(q, k, v, cos_table, sin_table, num_heads, num_kv_heads, head
     if s.dtype != c.dtype:
         s = s.to(c.dtype)
     out = torch.empty(B, S, num_heads * head_dim, dtype=q.dtype, device=q.device)
+    if S >= ROPE_PREPASS_MIN_SEQ:
+        # rotate q and k once into one [B, S, (Hq+Hkv)*D] buffer, then attention without RoPE: on
+        # load, every CTA would re-read the cos/sin rows of every key tile
+        hq, hkv = num_heads * head_dim, num_kv_heads * head_dim
+        qk = torch.empty(B, S, hq + hkv, dtype=q.dtype, device=q.device)
+        with call_ctx(dev):
+            _lib.check(_lib.lib().tk_rope_qk(
+                q3.data_ptr(), qs, k3.data_ptr(), ks, c.data_ptr(), s.data_ptr(), _lib.dtype_code(c.dtype),
+                c.shape[0], qk.data_ptr(), hq + hkv, B, S, num_heads, num_kv_heads, head_dim, int(start_pos),
+                _lib.dtype_code(q.dtype), _lib.stream_ptr(dev)), "tk_rope_qk", 1)
+            _lib.check(_lib.lib().tk_causal_attention(
+                qk.data_ptr(), hq + hkv, qk.data_ptr() + hq * qk.element_size(), hq + hkv, v3.data_ptr(), vs,
+                out.data_ptr(), hq, B, S, num_heads, num_kv_heads, head_dim, _lib.dtype_code(q.dtype),
+                _lib.stream_ptr(dev)), "tk_causal_attention", 1)
+        return out
     with call_ctx(dev):
         _lib.check(_lib.lib().tk_rope_attention(
             q3.data_ptr(), qs, k3.data_ptr(), ks, v3.data_ptr(), vs, c.data_ptr(), s.data_ptr(),
