@@ -150,6 +150,11 @@ TK_API int tk_causal_attention(const void* q, int64_t q_tok_stride, const void* 
  *                 the row_ssq_in of the next folded RMSNorm.
  *  rope_*         plain store only, rope_head_dim > 0: the columns [0, n0 + n1) (the q
  *                 and k heads) are rounded to dtype and rotated as in tk_linear_rope.
+ *  weights_prefetch  nonzero only if no kernel enqueued since the stream last waited for all
+ *                 earlier work writes the weights (e.g. inside a CUDA graph that never writes
+ *                 them): the first weight tiles are then loaded into shared memory before the
+ *                 previous kernel has finished (programmatic dependent launch). With 0 they are
+ *                 only prefetched into L2 until it has.
  */
 typedef struct tk_epilogue {
   const void* residual;
@@ -163,6 +168,7 @@ typedef struct tk_epilogue {
   const void* rope_cos;
   const void* rope_sin;
   int64_t rope_table_rows;
+  int weights_prefetch;
 } tk_epilogue;
 
 /*

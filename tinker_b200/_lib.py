@@ -30,7 +30,8 @@ class Epilogue(ctypes.Structure):
     """``tk_epilogue`` of tinker_b200.h: options of tk_linear_ex / tk_gate_up_swiglu_ex."""
     _fields_ = [("residual", _P), ("row_ssq_in", _P), ("row_ssq_parts", _I), ("row_ssq_eps", _F),
                 ("row_ssq_out", _P), ("rope_seq", _I), ("rope_start", _I), ("rope_head_dim", _I),
-                ("rope_cos", _P), ("rope_sin", _P), ("rope_table_rows", _I64)]
+                ("rope_cos", _P), ("rope_sin", _P), ("rope_table_rows", _I64),
+                ("weights_prefetch", _I)]
 
 
 _EPI = ctypes.POINTER(Epilogue)

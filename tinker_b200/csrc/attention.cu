@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
   } else if (warp >= ROPE_WARP0) {
     // ---------------- RoPE of the K tiles (rows t and t + 64) ----------------
     if constexpr (ROPE) {
+      pdl_wait();  // the tables may have been written by the previous kernel
       const int t = tid - ROPE_WARP0 * 32;
       for (int j = 0; j < n_kv; ++j) {
         const int i = 2 * j;
@@ -353,6 +354,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       const int64_t qpos = static_cast<int64_t>(p.start_pos) + q_row;
       const bool valid = active && q_row < p.seq;
       float c[32], sn[32];
+      pdl_wait();  // the tables may have been written by the previous kernel
       if (valid) rope_load_block(p, qpos, 0, D / 2, c, sn);  // in flight while the Q tile lands
       ok = mbar_wait(bars + B_Q_FULL, 0);
       if (ok && valid) {

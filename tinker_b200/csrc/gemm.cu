@@ -59,6 +59,9 @@ struct Params {
   // Plain store: ssq_out[(col / 32) * m + r] = sum of squares of the 32 stored (rounded)
   // values of row r from column col on, the input of a folded RMSNorm downstream.
   float* ssq_out;
+  // Nonzero: no kernel since the stream last waited for all earlier work wrote the weights,
+  // so their first tiles may go to shared memory before griddepcontrol.wait.
+  int weights_prefetch;
 };
 
 // 1/rms of input row `row` for a folded RMSNorm (1 when there is none or the row is padding).
@@ -278,19 +281,36 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
         }
       };
-      // The weights do not depend on the previous kernel: fill the ring with the first
-      // tile's weight tiles before waiting for that kernel, and load activations after.
+      auto prefetch_b = [&](int nt, int kb) {
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_prefetch_2d(&tb0, kb * BK, nt * (BN / 2));
+          tma_prefetch_2d(&tb1, kb * BK, nt * (BN / 2));
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_prefetch_2d(tb, kb * BK, row0);
+        }
+      };
+      // Pull the first tile's weight tiles into L2 while the previous kernel finishes; shared
+      // memory is only written after griddepcontrol.wait (a weight written by that kernel could
+      // still be in flight), so the ring fills from L2 right after it.
       int pre = 0;
       if (static_cast<int>(blockIdx.x) < total_tiles) {
         int mt0, nt0;
         tile_coords(blockIdx.x, p, mt0, nt0);
         pre = min(STAGES, p.num_kb);
+        if (!p.weights_prefetch) {
+          for (int kb = 0; kb < pre; ++kb) prefetch_b(nt0, kb);
+          pdl_wait();
+        }
         for (int kb = 0; kb < pre; ++kb) {
           mbar_arrive_expect_tx(&full[kb], S::A_BYTES + S::B_BYTES);
           load_b(kb, nt0, kb);
         }
+        if (p.weights_prefetch) pdl_wait();
+      } else {
+        pdl_wait();
       }
-      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -482,17 +502,33 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_2d_pair(sb, tb, full_bar(stage), kb * BK, row0 + rank * (BN / 2), pol_w);
         }
       };
+      auto prefetch_b = [&](int nt, int kb) {
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_prefetch_2d(rank == 0 ? &tb0 : &tb1, kb * BK, nt * (BN / 2));
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_prefetch_2d(tb, kb * BK, row0 + rank * (BN / 2));
+        }
+      };
+      // weight tiles into L2 before the wait, into shared memory after it (see gemm_kernel)
       int pre = 0;
       if (pair < total_tiles) {
         int mt0, nt0;
         tile_coords(pair, p, mt0, nt0);
         pre = min(STAGES, p.num_kb);
+        if (!p.weights_prefetch) {
+          for (int kb = 0; kb < pre; ++kb) prefetch_b(nt0, kb);
+          pdl_wait();
+        }
         for (int kb = 0; kb < pre; ++kb) {
           if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * S::STAGE);
           load_b(kb, nt0, kb);
         }
+        if (p.weights_prefetch) pdl_wait();
+      } else {
+        pdl_wait();
       }
-      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -683,13 +719,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_2d_hint(sb, tb, &full[stage], kb * BK, row0, pol_w);
         }
       };
-      // weight tiles first (independent of the previous kernel), activations after it completes
+      // weight tiles into L2 before the wait, into shared memory after it (see gemm_kernel)
       const int pre = min(stages, kb1 - kb0);
+      for (int i = 0; i < pre && !p.weights_prefetch; ++i) {
+        const int kb = kb0 + i;
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_prefetch_2d(&tb0, kb * BK, nt * (BN / 2));
+          tma_prefetch_2d(&tb1, kb * BK, nt * (BN / 2));
+        } else {
+          const CUtensorMap* tb = nt < p.seg1 ? &tb0 : (nt < p.seg2 ? &tb1 : &tb2);
+          const int row0 = nt < p.seg1 ? nt * BN : (nt < p.seg2 ? (nt - p.seg1) * BN : (nt - p.seg2) * BN);
+          tma_prefetch_2d(tb, kb * BK, row0);
+        }
+      }
+      if (!p.weights_prefetch) pdl_wait();
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], S::STAGE);
         load_b(i, kb0 + i);
       }
-      pdl_wait();
+      if (p.weights_prefetch) pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       for (int kb = kb0; kb < kb1; ++kb) {
@@ -1018,6 +1066,7 @@ struct Extras {
   int ssq_parts = 0;
   float ssq_inv_k = 0.f, ssq_eps = 0.f;
   float* ssq_out = nullptr;
+  int weights_prefetch = 0;
 };
 
 void apply_extras(Params& p, const Extras& e) {
@@ -1033,6 +1082,7 @@ void apply_extras(Params& p, const Extras& e) {
   p.ssq_inv_k = e.ssq_inv_k;
   p.ssq_eps = e.ssq_eps;
   p.ssq_out = e.ssq_out;
+  p.weights_prefetch = e.weights_prefetch;
 }
 
 template <int DT>
@@ -1215,6 +1265,7 @@ int extras_from(const tk_epilogue* e, int64_t m, int64_t k, int64_t n, int64_t r
     if (!plain_store) return fail_invalid("epilogue: row_ssq_out needs the plain store");
     ex->ssq_out = e->row_ssq_out;
   }
+  ex->weights_prefetch = e->weights_prefetch ? 1 : 0;
   if (e->rope_head_dim) {
     const int hd = e->rope_head_dim;
     if (!plain_store || hd < 32 || hd % 32 != 0 || rope_cols % hd != 0 || rope_cols > n)

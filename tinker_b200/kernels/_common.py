@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import contextlib
+import threading
 
 import torch
 
@@ -33,4 +34,26 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-__all__ = ["call_ctx", "rows_view", "row_stride", "ptr", "_lib"]
+_graph_state = threading.local()
+
+
+@contextlib.contextmanager
+def stable_weights():
+    """Inside this block the GEMMs may load their first weight tiles into shared memory before
+    the previous kernel has finished (programmatic dependent launch). Only valid where no kernel
+    enqueued since the stream last waited for all earlier work writes any weight: ``optimize``
+    wraps its CUDA-graph capture in it (no kernel of the captured forward writes a weight, and the
+    graph's first kernel is an ordinary launch)."""
+    prev = getattr(_graph_state, "stable", False)
+    _graph_state.stable = True
+    try:
+        yield
+    finally:
+        _graph_state.stable = prev
+
+
+def weights_are_stable() -> bool:
+    return getattr(_graph_state, "stable", False)
+
+
+__all__ = ["call_ctx", "rows_view", "row_stride", "ptr", "_lib", "stable_weights", "weights_are_stable"]

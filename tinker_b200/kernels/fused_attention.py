@@ -6,9 +6,8 @@ the same torch arithmetic, and ``fused_attention`` (:234-238) with the same
 arguments and result. Instead of the reference's three permute copies, two
 in-place RoPE launches and the attention launch (:195-231), one tcgen05 kernel
 reads q/k/v in their ``[batch, seq, heads * head_dim]`` projection layout,
-applies RoPE on load and writes the output in that layout; from
-``ROPE_PREPASS_MIN_SEQ`` on, one pass rotates q and k (``tk_rope_qk``) and the
-attention kernel runs without RoPE.
+applies RoPE on load and writes the output in that layout (the smallest
+problems), or runs after one pass that rotates q and k (``tk_rope_qk``).
 """
 
 from __future__ import annotations
@@ -19,9 +18,16 @@ from tinker_b200 import _lib
 from tinker_b200.kernels._common import call_ctx
 
 
-# From this sequence length on, fused_attention rotates q and k in a separate pass (tk_rope_qk)
-# and runs the attention kernel without RoPE; below it, one kernel rotates on load.
-ROPE_PREPASS_MIN_SEQ = 256
+# fused_attention rotates q and k in one separate pass (tk_rope_qk) and runs the attention kernel
+# without RoPE, except for the smallest problems (head_dim 64 and at most this many tokens), where
+# one kernel that rotates on load saves the extra launch. Rotating on load re-reads the cos/sin
+# rows of every key tile in every CTA, which costs more than the pass from there on (measured on
+# B200: equal at batch 8 x seq 128, head_dim 64; the pass is 1.3-2.6x faster at seq >= 512).
+ROPE_ON_LOAD_MAX_TOKENS = 1024
+
+
+def _rope_on_load(batch: int, seq: int, head_dim: int) -> bool:
+    return head_dim == 64 and batch * seq <= ROPE_ON_LOAD_MAX_TOKENS and seq <= 128
 
 
 def precompute_rope_tables(head_dim, max_seq_len, theta=10000.0, device=None, dtype=torch.float32):
@@ -69,7 +75,7 @@ def fused_attention(q, k, v, cos_table, sin_table, num_heads, num_kv_heads, head
     if s.dtype != c.dtype:
         s = s.to(c.dtype)
     out = torch.empty(B, S, num_heads * head_dim, dtype=q.dtype, device=q.device)
-    if S >= ROPE_PREPASS_MIN_SEQ:
+    if not _rope_on_load(B, S, head_dim):
         # rotate q and k once into one [B, S, (Hq+Hkv)*D] buffer, then attention without RoPE: on
         # load, every CTA would re-read the cos/sin rows of every key tile
         hq, hkv = num_heads * head_dim, num_kv_heads * head_dim

@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from tinker_b200 import _lib
-from tinker_b200.kernels._common import call_ctx, row_stride, rows_view
+from tinker_b200.kernels._common import call_ctx, row_stride, rows_view, weights_are_stable
 
 
 def _check_w(w: torch.Tensor, k: int, dtype) -> torch.Tensor:
@@ -43,9 +43,11 @@ def _check_x(x: torch.Tensor) -> torch.Tensor:
 
 def _epilogue(residual=None, row_ssq_in=None, row_ssq_eps=1e-6, row_ssq_out=None, rope=None):
     """A ``tk_epilogue`` for the ``_ex`` entry points (None when only the plain store is needed)."""
-    if residual is None and row_ssq_in is None and row_ssq_out is None and rope is None:
+    stable = weights_are_stable()
+    if residual is None and row_ssq_in is None and row_ssq_out is None and rope is None and not stable:
         return None
     e = _lib.Epilogue()
+    e.weights_prefetch = 1 if stable else 0
     e.residual = None if residual is None else residual.data_ptr()
     if row_ssq_in is not None:
         if row_ssq_in.dtype != torch.float32 or row_ssq_in.dim() != 2 or not row_ssq_in.is_contiguous():
@@ -152,7 +154,7 @@ def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.T
     _check_ssq(row_ssq_in, m, None, "row_ssq_in")
     out = torch.empty(m, n, dtype=x.dtype, device=x.device)
     with call_ctx(dev):
-        if row_ssq_in is None:
+        if row_ssq_in is None and not weights_are_stable():
             _lib.check(_lib.lib().tk_linear_rope(
                 x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0],
                 wv.data_ptr(), wv.shape[0], out.data_ptr(), n, m, k, S, int(start_pos), head_dim, c.data_ptr(),

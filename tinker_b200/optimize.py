@@ -20,6 +20,7 @@ import torch.nn as nn
 
 from tinker_b200 import _lib
 from tinker_b200.fusion import fuse_decoder_blocks, share_rope_tables
+from tinker_b200.kernels._common import stable_weights
 from tinker_b200.patch import patch_model
 
 
@@ -146,7 +147,8 @@ def _capture_cuda_graph(model, input_shape, vocab_size, verbose=False, clone_out
                 _ = model(static_input)
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            # no kernel of the forward writes a weight: the GEMMs may fetch weight tiles early
+            with torch.cuda.graph(graph), stable_weights():
                 static_output = model(static_input)
         if verbose:
             print(f"  [tinker] cuda graph captured (shape={input_shape})")
