@@ -225,12 +225,56 @@ def sweep_model1b(peaks, emit):
         torch.cuda.empty_cache()
 
 
+def run_case(spec: str, reps: int = 3):
+    """One configuration, eager, ``reps`` calls inside an NVTX range ``timed`` (for profilers):
+    ``rmsnorm:ROWS,H`` | ``ffn:T,H,F`` | ``attention:B,S,D,HQ,HKV`` (pre-rotated kernel) |
+    ``rope_attention:B,S,D,HQ,HKV`` (the drop-in entry), all bf16."""
+    from tinker_b200.kernels import causal_attention, fused_attention, fused_rmsnorm, precompute_rope_tables, swiglu_ffn
+    kind, _, args = spec.partition(":")
+    v = [int(a) for a in args.split(",")]
+    dt = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(3)
+    if kind == "rmsnorm":
+        x = torch.randn(v[0], v[1], device="cuda", generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(v[1], device="cuda", generator=g)).to(dt)
+        fn = lambda: fused_rmsnorm(x, w, 1e-6)
+    elif kind == "ffn":
+        t, h, f = v
+        x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        ws = [(0.02 * torch.randn(*sh, device="cuda", generator=g)).to(dt) for sh in ((f, h), (f, h), (h, f))]
+        fn = lambda: swiglu_ffn(x, *ws)
+    elif kind in ("attention", "rope_attention"):
+        b, s, d, hq, hkv = v
+        q = torch.randn(b, s, hq * d, device="cuda", generator=g).to(dt)
+        k = torch.randn(b, s, hkv * d, device="cuda", generator=g).to(dt)
+        vv = torch.randn(b, s, hkv * d, device="cuda", generator=g).to(dt)
+        cos, sin = precompute_rope_tables(d, s, device="cuda")
+        if kind == "attention":
+            fn = lambda: causal_attention(q, k, vv, hq, hkv, d)
+        else:
+            fn = lambda: fused_attention(q, k, vv, cos, sin, hq, hkv, d)
+    else:
+        raise ValueError(f"unknown case {spec}")
+    fn()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed")
+    for _ in range(reps):
+        fn()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="rmsnorm,ffn,attention,model1b")
     ap.add_argument("--dtypes", default="fp16,bf16")
+    ap.add_argument("--case", default=None, help="run one configuration for a profiler (see run_case)")
     args = ap.parse_args(argv)
     torch.cuda.set_device(0)
+    if args.case:
+        with torch.inference_mode():
+            run_case(args.case)
+        return
     peaks = _peaks()
     dtypes = [DTYPES[d] for d in args.dtypes.split(",")]
 
