@@ -40,7 +40,14 @@ constexpr int ROPE_WARP0 = 10;       // warps 10-11 rotate the K tiles (two rows
 constexpr int ROPE_K_THREADS = 64;
 constexpr float LAZY_RESCALE_LOG2 = 8.0f;  // move the running max only when it grows by more than 2^8
 
-__host__ __device__ constexpr int threads_for(bool rope) { return rope ? 384 : 320; }
+// Three warpgroups in both variants (without RoPE warps 10-11 only take part in set-up).
+// Registers: the kernel is compiled for LAUNCH_REGS per thread; after set-up the two
+// softmax warpgroups raise theirs to SOFTMAX_REGS and the TMA/MMA/RoPE warpgroup lowers its
+// own to OTHER_REGS (setmaxnreg). The split adds up to exactly the launch total, and the
+// host refuses to launch a build whose register count differs.
+__host__ __device__ constexpr int threads_for(bool) { return 384; }
+constexpr int LAUNCH_REGS = 168, SOFTMAX_REGS = 200, OTHER_REGS = 104;
+static_assert(2 * 128 * SOFTMAX_REGS + 128 * OTHER_REGS == 384 * LAUNCH_REGS, "register split must match the launch");
 
 template <int D>
 struct Smem {
@@ -200,6 +207,8 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp < 8) regs_increase<SOFTMAX_REGS>();
+  else regs_decrease<OTHER_REGS>();
 
   if (warp == TMA_WARP) {
     // ---------------- TMA producer: Q_a|Q_b, then K_0, V_0, K_1, V_1, ... ----------------
@@ -490,6 +499,9 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL),
                             "cudaFuncSetAttribute(attention)"))
       return rc;
+    cudaFuncAttributes fa{};
+    if (int rc = check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(attention)")) return rc;
+    if (fa.numRegs != LAUNCH_REGS) return set_error(TK_ERR_CUDA, "attention: unexpected register count");
     configured[dev.device] = true;
   }
   return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(threads_for(ROPE)), S::TOTAL, st, 1,
