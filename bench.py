@@ -50,7 +50,7 @@ def _args():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["forward", "gate_up_swiglu", "down_proj", "qkv_rope_proj", "o_proj",
-                                       "causal_attention", "rmsnorm", "qwen_forward"],
+                                       "causal_attention", "rmsnorm", "row_sumsq", "qwen_forward"],
                     help="profiling helper: time only the graph replay or one kernel kind (268M shapes), or "
                          "the Qwen-shaped batched forward (--qwen-batch sequences of 512)")
     ap.add_argument("--qwen-batch", type=int, default=64)
@@ -264,9 +264,13 @@ def _time_replays(graph, steps: int):
 
 def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
     """For each kernel kind of the forward: (one closure per layer launching it on that
-    layer's weights, algorithmic bytes per launch, flops per launch, launches per forward)."""
+    layer's weights, algorithmic bytes per launch, flops per launch, launches per forward).
+    The kinds are those of the fused, norm-folded decoder block: q|k|v with RoPE and the
+    attention RMSNorm in its epilogue, attention, o_proj + residual writing the row
+    statistics, gate|up + SwiGLU with the FFN RMSNorm in its epilogue, down + residual
+    writing the row statistics; plus the final RMSNorm and the first block's row statistics."""
     import torch
-    from tinker_b200.kernels import causal_attention, fused_rmsnorm, gate_up_swiglu, linear, linear_rope
+    from tinker_b200.kernels import causal_attention, fused_rmsnorm, gate_up_swiglu, linear, linear_rope, row_sumsq
     base = model._model if hasattr(model, "_model") else model
     layers = list(base.layers)
     M, H = tokens_per_fwd, cfg.hidden_size
@@ -279,24 +283,30 @@ def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
     a = torch.randn(M, hq * D, device=dev, generator=g).to(dt)
     qkv = torch.randn(1, M, (hq + 2 * hkv) * D, device=dev, generator=g).to(dt)
     x3 = x.view(1, M, H)
+    ssq_in = row_sumsq(x)
+    ssq_out = torch.empty(H // 32, M, dtype=torch.float32, device=dev)
+    ssq_b = 4 * M * (H // 32)
     S = M
+    L = len(layers)
     return {
-        "gate_up_swiglu": ([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight)
-                            for l in layers], 2 * F * H * es + M * H * es + M * F * es, 2 * M * H * 2 * F, len(layers)),
-        "down_proj": ([lambda l=l: linear(hbuf, l.ffn.down_proj.weight, residual=x) for l in layers],
-                      H * F * es + M * F * es + 2 * M * H * es, 2 * M * F * H, len(layers)),
+        "gate_up_swiglu": ([lambda l=l: gate_up_swiglu(x, l.ffn.gate_proj.weight, l.ffn.up_proj.weight,
+                                                       row_ssq_in=ssq_in, row_ssq_eps=cfg.eps) for l in layers],
+                           2 * F * H * es + M * H * es + M * F * es + ssq_b, 2 * M * H * 2 * F, L),
+        "down_proj": ([lambda l=l: linear(hbuf, l.ffn.down_proj.weight, residual=x, row_ssq_out=ssq_out)
+                       for l in layers], H * F * es + M * F * es + 2 * M * H * es + ssq_b, 2 * M * F * H, L),
         "qkv_rope_proj": ([lambda l=l: linear_rope(x3, l.attn.q_proj.weight, l.attn.k_proj.weight,
-                                                   l.attn.v_proj.weight, l.attn.cos_table, l.attn.sin_table, D)
+                                                   l.attn.v_proj.weight, l.attn.cos_table, l.attn.sin_table, D,
+                                                   row_ssq_in=ssq_in, row_ssq_eps=cfg.eps)
                            for l in layers],
-                          (hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es + 2 * S * (D // 2) * 4,
-                          2 * M * H * (hq + 2 * hkv) * D, len(layers)),
-        "o_proj": ([lambda l=l: linear(a, l.attn.o_proj.weight, residual=x) for l in layers],
-                   H * hq * D * es + M * hq * D * es + 2 * M * H * es, 2 * M * hq * D * H, len(layers)),
+                          (hq + 2 * hkv) * D * H * es + M * H * es + M * (hq + 2 * hkv) * D * es + 2 * S * (D // 2) * 4
+                          + ssq_b, 2 * M * H * (hq + 2 * hkv) * D, L),
+        "o_proj": ([lambda l=l: linear(a, l.attn.o_proj.weight, residual=x, row_ssq_out=ssq_out) for l in layers],
+                   H * hq * D * es + M * hq * D * es + 2 * M * H * es + ssq_b, 2 * M * hq * D * H, L),
         "causal_attention": ([lambda: causal_attention(qkv[..., :hq * D], qkv[..., hq * D:(hq + hkv) * D],
                                                        qkv[..., (hq + hkv) * D:], hq, hkv, D) for _ in layers],
-                             2 * S * D * (2 * hq + 2 * hkv), 2 * 2 * hq * D * S * S // 2, len(layers)),
-        "rmsnorm": ([lambda l=l: fused_rmsnorm(x, l.attn_norm.weight, 1e-6) for l in layers],
-                    M * H * 2 * es + H * es, 4 * M * H, 2 * len(layers) + 1),
+                             2 * S * D * (2 * hq + 2 * hkv), 2 * 2 * hq * D * S * S // 2, L),
+        "rmsnorm": ([lambda: fused_rmsnorm(x, base.norm.weight, cfg.eps)], M * H * 2 * es + H * es, 4 * M * H, 1),
+        "row_sumsq": ([lambda: row_sumsq(x)], M * H * es + ssq_b, 2 * M * H, 1),
     }
 
 
