@@ -157,3 +157,33 @@ def test_folded_norms_match_unfolded_and_follow_weight_updates():
         ya2, yb2 = a(tokens).float(), b(tokens).float()
     assert ((ya2 - ya).norm() / ya.norm()).item() > 1e-2
     assert ((ya2 - yb2).norm() / ya2.norm()).item() < 5e-3
+
+
+def test_folded_norm_statistics_follow_in_place_changes():
+    """The row statistics a folded block hands to the next one are recomputed when the hidden
+    states were changed in place in between (a model that scales the residual stream), which
+    the tensor's version counter shows outside inference mode."""
+    require_b200()
+    import torch.nn as nn
+    import tinker_b200
+    from tinker_b200.eager_model import TINY, build_model, make_tokens
+
+    class Scaled(nn.Module):  # x = block(x); x *= 1.5 (in place) between blocks
+        def __init__(self, lm):
+            super().__init__()
+            self.lm = lm
+
+        def forward(self, tokens):
+            x = self.lm.embedding(tokens)
+            for layer in self.lm.layers:
+                x = layer(x)
+                x.mul_(1.5)
+            return self.lm.output(self.lm.norm(x))
+
+    cfg = TINY.with_(num_layers=3)
+    tokens = make_tokens(cfg, 2, 64, seed=3).cuda()
+    a = Scaled(tinker_b200.optimize(build_model(cfg, seed=6).cuda(), dtype=torch.float16, fold_norms=False))
+    b = Scaled(tinker_b200.optimize(build_model(cfg, seed=6).cuda(), dtype=torch.float16, fold_norms=True))
+    with torch.no_grad():  # version counters exist outside inference mode
+        ya, yb = a(tokens).float(), b(tokens).float()
+    assert ((ya - yb).norm() / ya.norm()).item() < 5e-3

@@ -25,7 +25,11 @@ tensor; the first block computes them from its input) - 5 kernels per block:
     y   = down(g) + h                       -> rms statistics of y
 
 The result differs from norm-then-GEMM only by where the rounding to the model dtype
-happens (the weight product instead of the normalised activations). The replacement is
+happens (the weight product instead of the normalised activations). The statistics handed
+from one block to the next describe the output tensor as returned; a change made to it in
+place before the next block is detected through the tensor's version counter, except for
+inference tensors (``torch.inference_mode``), which have none - a model that rescales its
+residual stream in place between blocks under inference mode needs ``fold_norms=False``. The replacement is
 bound only after the block's own forward is shown to have exactly that
 dataflow: forward hooks substitute large random tensors for the outputs of the
 four children and record their inputs, and the block must feed ``x`` to norm1,
@@ -98,6 +102,10 @@ def _folded_weights(block):
     return folded
 
 
+def _version_of(t: torch.Tensor):
+    return None if t.is_inference() else t._version
+
+
 def _can_fold(block, x: torch.Tensor) -> bool:
     n1, at, n2, ff = (getattr(block, n) for n in block._tinker_block_parts)
     return (x.dim() == 3 and x.shape[-1] % 32 == 0 and at.cos_table.dtype == torch.float32
@@ -111,8 +119,15 @@ def _folded_forward(self, x: torch.Tensor) -> torch.Tensor:
     wq, wk, wv, wg, wu = _folded_weights(self)
     B, S, H = x.shape
     m = B * S
-    ssq_x = getattr(x, "_tinker_row_ssq", None)
-    if ssq_x is None or ssq_x.shape != (H // 32, m) or ssq_x.device != x.device:
+    stats = getattr(x, "_tinker_row_ssq", None)
+    ssq_x = None
+    if stats is not None:
+        ssq, version = stats
+        # valid only for the contents they were computed from: an in-place change since then
+        # shows in the version counter (inference tensors have none; see the module docstring)
+        if version == _version_of(x) and ssq.shape == (H // 32, m) and ssq.device == x.device:
+            ssq_x = ssq
+    if ssq_x is None:
         ssq_x = row_sumsq(x)
     hq, hkv = at.num_heads * at.head_dim, at.num_kv_heads * at.head_dim
     qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
@@ -124,7 +139,7 @@ def _folded_forward(self, x: torch.Tensor) -> torch.Tensor:
     g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)
     ssq_y = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
     y = linear(g, ff.down_proj.weight, residual=h, row_ssq_out=ssq_y)
-    y._tinker_row_ssq = ssq_y  # the next folded block reads the statistics from here
+    y._tinker_row_ssq = (ssq_y, _version_of(y))  # the next folded block reads the statistics from here
     return y
 
 
