@@ -40,14 +40,8 @@ constexpr int ROPE_WARP0 = 10;       // warps 10-11 rotate the K tiles (two rows
 constexpr int ROPE_K_THREADS = 64;
 constexpr float LAZY_RESCALE_LOG2 = 8.0f;  // move the running max only when it grows by more than 2^8
 
-// Three warpgroups in both variants (without RoPE warps 10-11 only take part in set-up).
-// Registers: the kernel is compiled for LAUNCH_REGS per thread; after set-up the two
-// softmax warpgroups raise theirs to SOFTMAX_REGS and the TMA/MMA/RoPE warpgroup lowers its
-// own to OTHER_REGS (setmaxnreg). The split adds up to exactly the launch total, and the
-// host refuses to launch a build whose register count differs.
+// Three warpgroups in both variants (without RoPE, warps 10-11 only take part in set-up).
 __host__ __device__ constexpr int threads_for(bool) { return 384; }
-constexpr int LAUNCH_REGS = 168, SOFTMAX_REGS = 200, OTHER_REGS = 104;
-static_assert(2 * 128 * SOFTMAX_REGS + 128 * OTHER_REGS == 384 * LAUNCH_REGS, "register split must match the launch");
 
 template <int D>
 struct Smem {
@@ -113,6 +107,25 @@ __device__ __forceinline__ float exp2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // RoPE of one row of a swizzled [128 x D] tile, in 64-column blocks: the 32 cos and
@@ -207,8 +220,6 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (warp < 8) regs_increase<SOFTMAX_REGS>();
-  else regs_decrease<OTHER_REGS>();
 
   if (warp == TMA_WARP) {
     // ---------------- TMA producer: Q_a|Q_b, then K_0, V_0, K_1, V_1, ... ----------------
@@ -407,13 +418,22 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       }
       // p = 2^(s * scale * log2(e) - m): one FMA and one MUFU.EX2 per score
       const float neg_m = -m_use;
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // packed f32x2 FMA / add: two scores per instruction
+      const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), negm2 = pack_f32x2(neg_m, neg_m);
+      uint64_t rs2[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        sv[c] = exp2_approx(fmaf(sv[c], p.scale_log2, neg_m));
-        rs8[c & 7] += sv[c];
+      for (int c = 0; c < BKV; c += 2) {
+        const uint64_t e = fma_f32x2(pack_f32x2(sv[c], sv[c + 1]), scale2, negm2);
+        float e0, e1;
+        unpack_f32x2(e, e0, e1);
+        sv[c] = exp2_approx(e0);
+        sv[c + 1] = exp2_approx(e1);
+        rs2[(c >> 1) & 3] = add_f32x2(rs2[(c >> 1) & 3], pack_f32x2(sv[c], sv[c + 1]));
       }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      float rp[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) unpack_f32x2(rs2[i], rp[2 * i], rp[2 * i + 1]);
+      const float rs = ((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7]));
       l_run = l_run * alpha + rs;
       m_run = m_use;
 
@@ -499,9 +519,6 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL),
                             "cudaFuncSetAttribute(attention)"))
       return rc;
-    cudaFuncAttributes fa{};
-    if (int rc = check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(attention)")) return rc;
-    if (fa.numRegs != LAUNCH_REGS) return set_error(TK_ERR_CUDA, "attention: unexpected register count");
     configured[dev.device] = true;
   }
   return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(threads_for(ROPE)), S::TOTAL, st, 1,
@@ -509,7 +526,8 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
 }
 
 // RoPE of q and k in one pass, into out [batch, seq, (num_heads + num_kv_heads) * D] (q heads,
-// then k heads): one thread per 8 consecutive elements (4 interleaved pairs) of a token row.
+// then k heads). One thread per (token, 8-column chunk of a head): it loads the 4 cos and 4 sin
+// values of its chunk once and rotates that chunk in every q and k head of the token.
 template <int DT>
 __global__ void __launch_bounds__(256) rope_qk_kernel(const void* __restrict__ q, int64_t qs,
                                                        const void* __restrict__ k, int64_t ks, void* __restrict__ out,
@@ -517,28 +535,31 @@ __global__ void __launch_bounds__(256) rope_qk_kernel(const void* __restrict__ q
   using Dx = Dt<DT>;
   pdl_launch_dependents();
   pdl_wait();  // q and k are written by the previous kernel
-  const int qcols = p.num_heads * head_dim;
-  const int vecs = (qcols + p.num_kv_heads * head_dim) / 8;
+  const int chunks = head_dim / 8;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= tokens * vecs) return;
-  const int64_t tok = t / vecs;
-  const int col = static_cast<int>(t - tok * vecs) * 8;
+  if (t >= tokens * chunks) return;
+  const int64_t tok = t / chunks;
+  const int col = static_cast<int>(t - tok * chunks) * 8;
   const int64_t pos = static_cast<int64_t>(p.start_pos) + tok % p.seq;
-  const uint16_t* src = col < qcols ? reinterpret_cast<const uint16_t*>(q) + tok * qs + col
-                                    : reinterpret_cast<const uint16_t*>(k) + tok * ks + (col - qcols);
-  const int i0 = (col % head_dim) / 2;
   float c[4], sn[4];
-  load_cs4(p.cos_t, p.table_dtype, pos * (head_dim / 2) + i0, c);
-  load_cs4(p.sin_t, p.table_dtype, pos * (head_dim / 2) + i0, sn);
-  const uint4 u = *reinterpret_cast<const uint4*>(src);
-  uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  load_cs4(p.cos_t, p.table_dtype, pos * (head_dim / 2) + col / 2, c);
+  load_cs4(p.sin_t, p.table_dtype, pos * (head_dim / 2) + col / 2, sn);
+  const uint16_t* qrow = reinterpret_cast<const uint16_t*>(q) + tok * qs + col;
+  const uint16_t* krow = reinterpret_cast<const uint16_t*>(k) + tok * ks + col;
+  uint16_t* orow = reinterpret_cast<uint16_t*>(out) + tok * os + col;
+  const int heads = p.num_heads + p.num_kv_heads;
+  for (int h = 0; h < heads; ++h) {
+    const uint16_t* src = h < p.num_heads ? qrow + h * head_dim : krow + (h - p.num_heads) * head_dim;
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 x = Dx::unpack(*reinterpret_cast<typename Dx::T2*>(&w[i]));
-    typename Dx::T2 o = Dx::pack(x.x * c[i] - x.y * sn[i], x.x * sn[i] + x.y * c[i]);
-    w[i] = *reinterpret_cast<uint32_t*>(&o);
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = Dx::unpack(*reinterpret_cast<typename Dx::T2*>(&w[i]));
+      typename Dx::T2 o = Dx::pack(x.x * c[i] - x.y * sn[i], x.x * sn[i] + x.y * c[i]);
+      w[i] = *reinterpret_cast<uint32_t*>(&o);
+    }
+    *reinterpret_cast<uint4*>(orow + h * head_dim) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + tok * os + col) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <bool ROPE>
@@ -664,7 +685,7 @@ extern "C" int tk_rope_qk(const void* q, int64_t q_tok_stride, const void* k, in
   p.sin_t = sin_table;
   p.table_dtype = table_dtype;
   const int64_t tokens = int64_t(batch) * seq;
-  const int64_t threads = tokens * (width / 8);
+  const int64_t threads = tokens * (head_dim / 8);
   const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TK_F16)

@@ -360,17 +360,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   tmem_st32u(taddr, u);
 }
 
-// ---- per-warpgroup register budgets (all four warps of a warpgroup execute the same one;
-// the increases and decreases of a CTA must add up to the registers it was launched with) ----
-template <uint32_t R>
-__device__ __forceinline__ void regs_increase() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
-}
-template <uint32_t R>
-__device__ __forceinline__ void regs_decrease() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
-}
-
 // ---- programmatic dependent launch -------------------------------------------------
 // Allow the next kernel in the stream to start launching (its set-up then overlaps
 // this kernel). Issued once per CTA, after the CTA holds its TMEM, so a dependent
