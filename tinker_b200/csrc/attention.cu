@@ -23,6 +23,7 @@
 // Causal tiles above the diagonal are skipped. The arithmetic follows
 // _attention_kernel (tinker/kernels/fused_attention.py:74-154): scale
 // 1/sqrt(head_dim), running max / sum in fp32, output divided by the sum.
+#include <algorithm>
 #include <cmath>
 
 #include "tk_common.cuh"
@@ -526,20 +527,26 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
 }
 
 // RoPE of q and k in one pass, into out [batch, seq, (num_heads + num_kv_heads) * D] (q heads,
-// then k heads). One thread per (token, 8-column chunk of a head): it loads the 4 cos and 4 sin
-// values of its chunk once and rotates that chunk in every q and k head of the token.
+// then k heads). One thread per (token, group of heads_per_thread heads, 8-column chunk of a
+// head): it loads the 4 cos and 4 sin values of its chunk once and rotates that chunk in each
+// head of its group (few heads per thread when there are few tokens, all of them when many).
 template <int DT>
 __global__ void __launch_bounds__(256) rope_qk_kernel(const void* __restrict__ q, int64_t qs,
                                                        const void* __restrict__ k, int64_t ks, void* __restrict__ out,
-                                                       int64_t os, Params p, int head_dim, int64_t tokens) {
+                                                       int64_t os, Params p, int head_dim, int64_t tokens,
+                                                       int heads_per_thread) {
   using Dx = Dt<DT>;
   pdl_launch_dependents();
   pdl_wait();  // q and k are written by the previous kernel
   const int chunks = head_dim / 8;
+  const int heads = p.num_heads + p.num_kv_heads;
+  const int groups = (heads + heads_per_thread - 1) / heads_per_thread;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= tokens * chunks) return;
-  const int64_t tok = t / chunks;
-  const int col = static_cast<int>(t - tok * chunks) * 8;
+  if (t >= tokens * groups * chunks) return;
+  const int64_t tok = t / (groups * chunks);
+  const int rem = static_cast<int>(t - tok * groups * chunks);
+  const int grp = rem / chunks;
+  const int col = (rem - grp * chunks) * 8;
   const int64_t pos = static_cast<int64_t>(p.start_pos) + tok % p.seq;
   float c[4], sn[4];
   load_cs4(p.cos_t, p.table_dtype, pos * (head_dim / 2) + col / 2, c);
@@ -547,8 +554,8 @@ __global__ void __launch_bounds__(256) rope_qk_kernel(const void* __restrict__ q
   const uint16_t* qrow = reinterpret_cast<const uint16_t*>(q) + tok * qs + col;
   const uint16_t* krow = reinterpret_cast<const uint16_t*>(k) + tok * ks + col;
   uint16_t* orow = reinterpret_cast<uint16_t*>(out) + tok * os + col;
-  const int heads = p.num_heads + p.num_kv_heads;
-  for (int h = 0; h < heads; ++h) {
+  const int h1 = min(heads, (grp + 1) * heads_per_thread);
+  for (int h = grp * heads_per_thread; h < h1; ++h) {
     const uint16_t* src = h < p.num_heads ? qrow + h * head_dim : krow + (h - p.num_heads) * head_dim;
     const uint4 u = *reinterpret_cast<const uint4*>(src);
     uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -685,12 +692,21 @@ extern "C" int tk_rope_qk(const void* q, int64_t q_tok_stride, const void* k, in
   p.sin_t = sin_table;
   p.table_dtype = table_dtype;
   const int64_t tokens = int64_t(batch) * seq;
-  const int64_t threads = tokens * (head_dim / 8);
+  // enough threads to fill the GPU (~8 blocks of 256 per SM), as many heads per thread as that allows
+  const int heads = num_heads + num_kv_heads;
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  const int64_t want = int64_t(dev.sm_count) * 8 * 256;
+  const int64_t per_head = tokens * (head_dim / 8);
+  const int hpt_max = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(heads, per_head * heads / want)));
+  const int groups = (heads + hpt_max - 1) / hpt_max;
+  const int hpt = (heads + groups - 1) / groups;  // equal groups
+  const int64_t threads = per_head * groups;
   const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TK_F16)
     return launch_kernel(attn::rope_qk_kernel<TK_F16>, grid, block, 0, st, 1, "rope_qk_kernel", q, q_tok_stride, k,
-                         k_tok_stride, out, out_tok_stride, p, head_dim, tokens);
+                         k_tok_stride, out, out_tok_stride, p, head_dim, tokens, hpt);
   return launch_kernel(attn::rope_qk_kernel<TK_BF16>, grid, block, 0, st, 1, "rope_qk_kernel", q, q_tok_stride, k,
-                       k_tok_stride, out, out_tok_stride, p, head_dim, tokens);
+                       k_tok_stride, out, out_tok_stride, p, head_dim, tokens, hpt);
 }
