@@ -33,6 +33,11 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of 2-byte elements
 constexpr int THREADS = 192;
+// 2-SM pair kernel: warps 0 (TMA), 1 (MMA) and eight epilogue warps, two per TMEM lane quarter
+// (each covers half of the tile's columns), so the epilogue of tile i keeps pace with the
+// main loop of tile i + 1 even when K is short.
+constexpr int PAIR_THREADS = 320;
+constexpr int PAIR_EPI_WARPS = 8;
 constexpr int GROUP_M = 16;  // rasterisation: GROUP_M m-tiles sweep all n-tiles together
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1 };
@@ -94,8 +99,9 @@ struct Smem {
                                                          : (2 * BN) <= 256 ? 256 : 512;
 };
 
-// silu(g) * u in fp32, as the SwiGLU epilogue has always computed it.
-__device__ __forceinline__ float swiglu_f(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+// silu(g) * u = g / (1 + e^-g) * u in fp32 with the fast exponential and division (a few ulp of
+// fp32; the result is rounded to 16 bits right after).
+__device__ __forceinline__ float swiglu_f(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
 __device__ __forceinline__ void scale32(float (&v)[32], float s) {
   if (s != 1.f) {
@@ -440,7 +446,7 @@ struct PairSmem {
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;  // shared::cluster address of the same offset in the pair leader
 
 template <int DT, int BN, int EPI, int STAGES>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(PAIR_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
                      const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tb2, const Params p) {
   using S = PairSmem<BN, STAGES>;
@@ -468,7 +474,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // four epilogue warps in each CTA of the pair
+      mbar_init(&tempty[a], 2 * PAIR_EPI_WARPS);  // every epilogue warp of both CTAs of the pair
     }
     fence_mbar_init();
   }
@@ -576,6 +582,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;  // which half of the tile's columns this warp stores
     const int row_in_tile = rank * 128 + quarter * 32 + lane;
     const uint32_t tempty_leader = smem_u32(&tempty[0]) & kPeerBitMask;
     int i = 0;
@@ -590,8 +597,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = mt * 256 + row_in_tile;
       const float rs = row_rstd(p, row);
       if constexpr (EPI == EPI_SWIGLU) {
+        static_assert(BN % 128 == 0, "each half of the SwiGLU columns must be whole 32-column chunks");
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = half * (BN / 4); c < (half + 1) * (BN / 4); c += 32) {
           float g[32], u[32];
           tmem_load32x2(taddr + c, taddr + BN / 2 + c, g, u);
 #pragma unroll
@@ -599,8 +607,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (row < p.m) store_row32<DT>(p.y, p.ldy, row, nt * (BN / 2) + c, p.n, g, nullptr);
         }
       } else {
+        static_assert(BN % 64 == 0, "each half of the columns must be whole 32-column chunks");
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
           float v[32];
           tmem_load32(taddr + c, v);
           scale32(v, rs);
@@ -905,7 +914,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
       return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(THREADS);
+    cfg.blockDim = dim3(PAIR_THREADS);
     cfg.dynamicSmemBytes = S::TOTAL;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -920,7 +929,8 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int pairs = std::max(1, std::min(tiles, max_pairs[dev.device]));
-  return launch_kernel(kern, dim3(2 * pairs), dim3(THREADS), S::TOTAL, st, 2, "gemm_pair_kernel", ta, tb0, tb1, tb2, p);
+  return launch_kernel(kern, dim3(2 * pairs), dim3(PAIR_THREADS), S::TOTAL, st, 2, "gemm_pair_kernel", ta, tb0, tb1, tb2,
+                       p);
 }
 
 // Pair (2-SM) tiles pay off once there are enough 256-row tiles to keep every SM pair busy.
