@@ -14,7 +14,10 @@ the token ids copied from pinned host memory and the logits copied back.
 
 Also reported: ``batched`` - Qwen2.5-0.5B-shaped bf16 prefill of batch 64 x
 seq 512, the 64 sequences split into contiguous blocks of 64/N per rank
-(aggregate tokens/s); ``roofline`` for the kernel with the largest share of the
+(aggregate tokens/s); ``decode`` - cached greedy decoding of the 268M decoder
+(KV cache, one CUDA graph per token) at batch 1 and 64 after a 128-token
+prompt, and the KV-cache attention kernel alone at batch 64 x 2048 cached
+positions; ``roofline`` for the kernel with the largest share of the
 forward; ``cpu_baseline`` - the numpy oracle's fp32 forward on the host cores.
 
 ``--impl reference`` times the reference's CPU path (the numpy restatement of
@@ -50,9 +53,12 @@ def _args():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["forward", "gate_up_swiglu", "down_proj", "qkv_rope_proj", "o_proj",
-                                       "causal_attention", "rmsnorm", "row_sumsq", "qwen_forward"],
-                    help="profiling helper: time only the graph replay or one kernel kind (268M shapes), or "
-                         "the Qwen-shaped batched forward (--qwen-batch sequences of 512)")
+                                       "causal_attention", "rmsnorm", "row_sumsq", "qwen_forward", "decode",
+                                       "kv_attention"],
+                    help="profiling helper: time only the graph replay or one kernel kind (268M shapes), "
+                         "the Qwen-shaped batched forward (--qwen-batch sequences of 512), cached decoding "
+                         "(decode) or the KV-cache attention kernel alone (kv_attention)")
+    ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--qwen-batch", type=int, default=64)
     ap.add_argument("--sweep", default=None, metavar="KINDS",
                     help="run the standalone sweeps instead (comma list of rmsnorm, ffn, attention, model1b; "
@@ -371,6 +377,124 @@ def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
     return table, roof
 
 
+DECODE_PROMPT, DECODE_NEW = 128, 128
+
+
+def _decode_bench(dev, peaks, peak_note, batch: int, prompt: int = DECODE_PROMPT, new: int = DECODE_NEW):
+    """Cached greedy decoding of the 268M decoder: a ``prompt``-token prefill, then ``new`` steps,
+    each one CUDA graph replay fed the previous step's argmax. ``value``: device-resident steps
+    (the argmax stays on the GPU); ``e2e``: every step copies its token ids from pinned host memory
+    and the chosen ids back."""
+    import torch
+    import tinker_b200
+    from tinker_b200 import _lib
+    from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
+    cfg = LLAMA_268M
+    model = tinker_b200.optimize(build_model(cfg, seed=0).to(dev), dtype=torch.float16, cuda_graph=False)
+    dec = tinker_b200.CachedDecoder(model, batch_size=batch, capacity=prompt + new + 1)
+    ids = make_tokens(cfg, batch, prompt, seed=1).to(dev)
+    with torch.inference_mode():
+        probe = tinker_b200.CachedDecoder(model, batch_size=batch, capacity=4, cuda_graph=False)
+        probe.prefill(ids[:, :1])
+        n0 = _lib.launch_counter[0]
+        probe.decode(ids[:, 1])
+        launches = _lib.launch_counter[0] - n0
+        del probe
+        for _ in range(2):  # warm-up, captures the step graph
+            dec.reset()
+            lg = dec.prefill(ids)
+            for _ in range(8):
+                lg = dec.decode(lg.argmax(-1))
+        dec.reset()
+        lg = dec.prefill(ids)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(new):
+            lg = dec.decode(lg.argmax(-1))
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / new
+        dec.reset()
+        lg = dec.prefill(ids)
+        tok_host = lg.argmax(-1).cpu().pin_memory()
+        ids_host = torch.empty_like(tok_host).pin_memory()
+        torch.cuda.synchronize()
+        per = []
+        for _ in range(new):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            lg = dec.decode(tok_host.to(dev, non_blocking=True))
+            ids_host.copy_(lg.argmax(-1), non_blocking=True)
+            b.record()
+            b.synchronize()
+            per.append(a.elapsed_time(b))
+            tok_host.copy_(ids_host)
+    e2e_ms = statistics.mean(per)
+    kv_len = prompt + new // 2  # mean cache length over the timed steps
+    weights = sum(p.numel() * p.element_size() for p in model.parameters()) \
+        - model.embedding.weight.numel() * model.embedding.weight.element_size()
+    kv_bytes = cfg.num_layers * 2 * batch * cfg.num_kv_heads * kv_len * cfg.head_dim * 2
+    step_bytes = weights + kv_bytes
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    out = {"metric": f"decode tokens/s @268M b{batch} (KV cache, {prompt}-token prompt, {new} new tokens, "
+                     "CUDA graph per step)",
+           "value": round(batch / (ms * 1e-3)), "unit": "tokens/s", "ms_per_step": round(ms, 4), "batch": batch,
+           "e2e": {"value": round(batch / (e2e_ms * 1e-3)), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": batch * 8, "d2h_bytes_per_step": batch * 8},
+           "roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": round(gbs, 1),
+                        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3),
+                        "note": f"weights (without the embedding) + K/V cache at the mean length {kv_len}, "
+                                f"{peak_note}"},
+           "gpu_launches_per_step": launches}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def _kv_attention_bench(dev, peaks, peak_note, steps: int = 50, batch: int = 64, kv_len: int = 2048):
+    """The KV-cache attention kernel alone on a bandwidth-sized decode step: ``batch`` sequences of
+    the 268M heads (16 q / 4 kv, head_dim 64) with ``kv_len - 1`` cached positions and one new
+    token; caches rotated so that the inputs exceed L2 between launches."""
+    import torch
+    from tinker_b200.kernels.kv_cache import kv_attention, kv_attention_workspace
+    from tinker_b200.kernels.fused_attention import precompute_rope_tables
+    hq, hkv, d = 16, 4, 64
+    g = torch.Generator(device=dev).manual_seed(3)
+    n_sets = 3  # 3 x 134 MB of cache > L2
+    caches = [(torch.randn(batch, hkv, kv_len, d, device=dev, generator=g).half(),
+               torch.randn(batch, hkv, kv_len, d, device=dev, generator=g).half()) for _ in range(n_sets)]
+    qkv = torch.randn(batch, 1, (hq + 2 * hkv) * d, device=dev, generator=g).half()
+    q, k, v = qkv[..., :hq * d], qkv[..., hq * d:(hq + hkv) * d], qkv[..., (hq + hkv) * d:]
+    cos, sin = precompute_rope_tables(d, kv_len, device=dev)
+    ws = torch.zeros(kv_attention_workspace(batch, hq, hkv, d, 1, kv_len), dtype=torch.uint8, device=dev)
+    start = kv_len - 1
+
+    def call(i):
+        kc, vc = caches[i % n_sets]
+        kv_attention(q, k, v, cos, sin, kc, vc, hq, hkv, d, start_pos=start, workspace=ws)
+
+    for i in range(5):
+        call(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    e0.record()
+    for i in range(steps):
+        call(i)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / steps * 1e3
+    nbytes = 2 * batch * hkv * kv_len * d * 2 + qkv.numel() * 2 + batch * hq * d * 2
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del caches
+    torch.cuda.empty_cache()
+    return {"kernel": "kv_attention", "case": f"b{batch} kv_len {kv_len} 16q/4kv d64 fp16, 1 new token",
+            "us": round(us, 2), "bytes": nbytes, "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3), "note": peak_note}
+
+
 def run_only(args):
     """Profiling helper: run just one forward replay loop, or one kernel kind, on the 268M
     shapes (``--only forward`` / ``--only gate_up_swiglu`` ...) and print its mean time."""
@@ -379,6 +503,15 @@ def run_only(args):
     from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.only in ("decode", "kv_attention"):
+        peaks, peak_note = _peaks()
+        if args.only == "decode":
+            for b in (1, 64):
+                print(json.dumps({"only": "decode", **_decode_bench(dev, peaks, peak_note, b)}), flush=True)
+        else:
+            print(json.dumps({"only": "kv_attention", **_kv_attention_bench(dev, peaks, peak_note, args.steps)}),
+                  flush=True)
+        return
     if args.only == "qwen_forward":
         from tinker_b200.eager_model import QWEN25_05B_SHAPED
         qcfg = QWEN25_05B_SHAPED
@@ -525,6 +658,16 @@ def run_ours(args):
         del qm
         torch.cuda.empty_cache()
 
+    # ---- cached decoding (each rank its own replica) ---------------------------------------------
+    decode = None
+    if not args.no_decode:
+        decode = [_decode_bench(dev, peaks, peak_note, b) for b in (1, 64)]
+        for d_ in decode:  # whole job: every replica's tokens over the slowest replica's step time
+            d_["ms_per_step"] = round(_max_over_ranks(d_["ms_per_step"], world, dev), 4)
+            d_["value"] = round(world * d_["batch"] / (d_["ms_per_step"] * 1e-3))
+            d_["n_gpus"] = world
+        decode.append(_kv_attention_bench(dev, peaks, peak_note))
+
     # ---- CPU baseline (rank 0 at N=1) ----------------------------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -549,7 +692,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": 128 * cfg.vocab_size * 2},
             "roofline": roof, "roofline_forward": roof_fwd, "kernels": table,
             "gpu_launches": launches_per_fwd * args.steps, "gpu_launches_per_fwd": launches_per_fwd,
-            "clocks": clocks, "cpu_baseline": cpu, "batched": batched,
+            "clocks": clocks, "cpu_baseline": cpu, "batched": batched, "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

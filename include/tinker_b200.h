@@ -50,8 +50,9 @@ TK_API const char* tk_last_error(void);
 TK_API int tk_check_device(int device);
 
 /* Read (and optionally clear) the sticky device-side error word of the current
- * device. Non-zero means a kernel's bounded wait gave up (1 = timeout) and its
- * outputs are invalid. Synchronises the device; meant for tests and debugging. */
+ * device. Non-zero means a kernel gave up and its outputs are invalid: 1 = a
+ * bounded wait timed out, 2 = a position read from device memory lay beyond a KV
+ * cache or RoPE table. Synchronises the device; meant for tests and debugging. */
 TK_API int tk_device_error(int* code, int clear);
 
 /*
@@ -135,6 +136,47 @@ TK_API int tk_rope_qk(const void* q, int64_t q_tok_stride, const void* k, int64_
 TK_API int tk_causal_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
                         const void* v, int64_t v_tok_stride, void* out, int64_t out_tok_stride, int batch,
                         int seq, int num_heads, int num_kv_heads, int head_dim, int dtype, void* stream);
+
+/*
+ * Attention of S new tokens per sequence against a KV cache (decode steps, short
+ * chunks), one launch: RoPE of the new q and k rows at positions start..start+S-1
+ * (float32 tables [table_rows, head_dim/2], results rounded to dtype), the append of
+ * the rotated k rows and the v rows to the cache, and causal GQA attention of the new
+ * rows over cache positions 0..start+S-1. Equals rows start..start+S-1 of the
+ * reference's causal RoPE attention over the whole sequence
+ * (tinker/kernels/fused_attention.py:176-192, :195-231), which has no cache and
+ * recomputes the sequence (tinker/modules/attention.py:51, README.md:102).
+ * q [batch*seq, >= num_heads*head_dim], k/v [batch*seq, >= num_kv_heads*head_dim]
+ * (projections without RoPE, token strides in elements); k_cache/v_cache
+ * [batch, num_kv_heads, capacity, head_dim] contiguous; out like q.
+ * start_pos_device: if not NULL the position is read from this device int at run
+ * time (a CUDA graph replays for every step); a position with start+S beyond the
+ * cache or the table then records device error 2 and leaves out unchanged.
+ * workspace: zero-filled device memory of tk_kv_attention_workspace() bytes (may be
+ * 0: then NULL is fine); the kernel returns it to zeros, so it is reused without a
+ * memset, but launches that overlap on the GPU must not share it.
+ */
+TK_API int tk_kv_attention(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride, const void* v,
+                           int64_t v_tok_stride, void* k_cache, void* v_cache, int capacity, const float* cos_table,
+                           const float* sin_table, int64_t table_rows, void* out, int64_t out_tok_stride, int batch,
+                           int seq, int num_heads, int num_kv_heads, int head_dim, int start_pos,
+                           const int* start_pos_device, void* workspace, int64_t workspace_bytes, int dtype,
+                           void* stream);
+
+/* Workspace bytes tk_kv_attention needs for these sizes when start+S <= max_kv
+ * (pass the cache capacity when the position comes from device memory). 0 when
+ * none is needed or the sizes are invalid, -1 without a device. */
+TK_API int64_t tk_kv_attention_workspace(int batch, int num_heads, int num_kv_heads, int head_dim, int seq,
+                                         int max_kv);
+
+/*
+ * Copy S rows of k (already rotated) and v per sequence into a KV cache at
+ * start_pos: the cache fill after a prompt's tk_linear_rope + tk_causal_attention.
+ * Layouts as tk_kv_attention.
+ */
+TK_API int tk_kv_append(const void* k, int64_t k_tok_stride, const void* v, int64_t v_tok_stride, void* k_cache,
+                        void* v_cache, int capacity, int batch, int seq, int num_kv_heads, int head_dim,
+                        int start_pos, int dtype, void* stream);
 
 /*
  * Epilogue options of tk_linear_ex / tk_gate_up_swiglu_ex (zero-initialise, then set):

@@ -3,7 +3,8 @@
 TEST INFRASTRUCTURE ONLY. This package restates, in numpy, the reference's
 eager PyTorch algorithm for every function on the hot path (RoPE tables,
 interleaved RoPE, causal GQA attention, RMSNorm, SwiGLU and the Llama-style
-decoder forward the reference benchmarks). It is the checker that the CUDA
+decoder forward the reference benchmarks), plus the rows of that attention a
+KV-cache decode step returns (``attention_rows``, pinned to ``attention``). It is the checker that the CUDA
 path is compared against, and the CPU baseline that ``bench.py`` times. Only
 ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs may import
 it; the product package ``tinker_b200`` never does.
@@ -19,6 +20,7 @@ from oracle.ops import (  # noqa: F401
     rope_tables,
     apply_rope,
     attention,
+    attention_rows,
     rmsnorm,
     add_rmsnorm,
     swiglu,

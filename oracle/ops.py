@@ -110,6 +110,47 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cos: np.ndarray, sin:
     return round_to(out, io_dtype) if io_dtype != F32 else out.astype(np.float32)
 
 
+def attention_rows(q: np.ndarray, k: np.ndarray, v: np.ndarray, cos: np.ndarray, sin: np.ndarray,
+                   num_heads: int, num_kv_heads: int, head_dim: int, start_pos: int,
+                   io_dtype: str = F32, acc=np.float64) -> np.ndarray:
+    """Rows ``start_pos .. start_pos+S-1`` of :func:`attention` over a whole sequence.
+
+    ``q[B,S,Hq*D]`` holds the queries of those positions only; ``k/v[B,start_pos+S,Hkv*D]`` all
+    keys and values of the sequence (none rotated yet). The arithmetic is that of
+    ``_attention_pytorch`` (tinker/kernels/fused_attention.py:176-192) with RoPE at absolute
+    positions (:165-173) and the causal mask of ``is_causal=True`` (query at position p sees keys
+    0..p, the kernel's ``q >= kv`` at :132), restricted to the last S query rows: what a decode
+    step with a KV cache must return, which the reference (no cache) obtains by running the
+    whole sequence.
+    """
+    B, S, _ = q.shape
+    L = k.shape[1]
+    if L != start_pos + S:
+        raise ValueError("k/v must hold positions 0 .. start_pos + S - 1")
+    groups = num_heads // num_kv_heads
+    qh = q.reshape(B, S, num_heads, head_dim).transpose(0, 2, 1, 3)
+    kh = k.reshape(B, L, num_kv_heads, head_dim).transpose(0, 2, 1, 3)
+    vh = v.reshape(B, L, num_kv_heads, head_dim).transpose(0, 2, 1, 3)
+    qh = apply_rope(qh, cos, sin, start_pos, out_dtype=io_dtype)
+    kh = apply_rope(kh, cos, sin, 0, out_dtype=io_dtype)
+    if groups > 1:
+        kh = np.repeat(kh, groups, axis=1)
+        vh = np.repeat(vh, groups, axis=1)
+    qh = np.asarray(qh, dtype=acc)
+    kh = np.asarray(kh, dtype=acc)
+    vh = np.asarray(vh, dtype=acc)
+    scale = 1.0 / np.sqrt(head_dim)
+    scores = np.matmul(qh, kh.transpose(0, 1, 3, 2)) * scale
+    mask = np.arange(L)[None, :] > (start_pos + np.arange(S))[:, None]
+    scores = np.where(mask[None, None], -np.inf, scores)
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    p = np.exp(scores)
+    p = p / p.sum(axis=-1, keepdims=True)
+    out = np.matmul(p, vh)
+    out = out.transpose(0, 2, 1, 3).reshape(B, S, num_heads * head_dim)
+    return round_to(out, io_dtype) if io_dtype != F32 else out.astype(np.float32)
+
+
 def rmsnorm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-6, out_dtype: str = F32,
             acc=np.float32) -> np.ndarray:
     """``y = x * rsqrt(mean(x^2) + eps) * w`` over the last axis.

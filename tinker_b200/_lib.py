@@ -56,7 +56,14 @@ SIGNATURES = {
     "tk_row_sumsq": [_P, _I64, _I64, _I64, _P, _I, _P],
     "tk_swiglu_ffn": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_swiglu_ffn_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
+    "tk_kv_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _I, _I,
+                        _P, _P, _I64, _I, _P],
+    "tk_kv_attention_workspace": [_I, _I, _I, _I, _I, _I],
+    "tk_kv_append": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
 }
+
+# entry points whose return value is not a status
+RESTYPES = {"tk_kv_attention_workspace": _I64}
 
 _lock = threading.Lock()
 _lib = None
@@ -82,7 +89,7 @@ def lib() -> ctypes.CDLL:
             for name, argtypes in SIGNATURES.items():
                 fn = getattr(L, name)
                 fn.argtypes = argtypes
-                fn.restype = _I
+                fn.restype = RESTYPES.get(name, _I)
             L.tk_last_error.argtypes = []
             L.tk_last_error.restype = ctypes.c_char_p
             _lib = L
@@ -132,7 +139,8 @@ def stream_ptr(device: torch.device) -> int:
 
 
 def device_error(clear: bool = True) -> int:
-    """Sticky device-side error word (non-zero: a kernel's bounded wait timed out)."""
+    """Sticky device-side error word (0: none; 1: a bounded wait timed out; 2: a device-side
+    position beyond a KV cache or RoPE table)."""
     code = _I(0)
     check(lib().tk_device_error(ctypes.byref(code), 1 if clear else 0), "tk_device_error")
     return code.value

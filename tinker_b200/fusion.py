@@ -73,9 +73,11 @@ def _takes_hidden_states_only(block: nn.Module) -> bool:
     return len(required) == 1
 
 
-def _fused_forward(self, x: torch.Tensor) -> torch.Tensor:
+def _fused_forward(self, x: torch.Tensor, kv_cache=None, start_pos: int = 0,
+                   position: torch.Tensor | None = None) -> torch.Tensor:
     n1, at, n2, ff = self._tinker_block_parts
-    h = getattr(self, at)(getattr(self, n1)(x), residual=x)
+    h = getattr(self, at)(getattr(self, n1)(x), start_pos=start_pos, residual=x, kv_cache=kv_cache,
+                          position=position)
     return getattr(self, ff)(getattr(self, n2)(h), residual=h)
 
 
@@ -112,9 +114,12 @@ def _can_fold(block, x: torch.Tensor) -> bool:
             and at.sin_table.dtype == torch.float32 and at.head_dim % 32 == 0)
 
 
-def _folded_forward(self, x: torch.Tensor) -> torch.Tensor:
+def _folded_forward(self, x: torch.Tensor, kv_cache=None, start_pos: int = 0,
+                    position: torch.Tensor | None = None) -> torch.Tensor:
+    """The block's forward; with ``kv_cache`` (a ``KVCacheLayer``) x holds new tokens from
+    ``start_pos`` (or the device ``position``) on that attend to, and are appended to, the cache."""
     if not _can_fold(self, x):
-        return _fused_forward(self, x)
+        return _fused_forward(self, x, kv_cache, start_pos, position)
     n1, at, n2, ff = (getattr(self, n) for n in self._tinker_block_parts)
     wq, wk, wv, wg, wu = _folded_weights(self)
     B, S, H = x.shape
@@ -130,10 +135,14 @@ def _folded_forward(self, x: torch.Tensor) -> torch.Tensor:
     if ssq_x is None:
         ssq_x = row_sumsq(x)
     hq, hkv = at.num_heads * at.head_dim, at.num_kv_heads * at.head_dim
-    qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
-                      row_ssq_eps=n1.eps)
-    a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
-                         at.num_kv_heads, at.head_dim)
+    if kv_cache is not None:
+        a = at.cached_attention(x, wq, wk, wv, kv_cache, start_pos, position, row_ssq_in=ssq_x,
+                                row_ssq_eps=n1.eps)
+    else:
+        qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
+                          row_ssq_eps=n1.eps)
+        a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
+                             at.num_kv_heads, at.head_dim)
     ssq_h = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
     h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h)
     g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)

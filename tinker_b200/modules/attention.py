@@ -16,6 +16,12 @@ import torch.nn as nn
 
 from tinker_b200.kernels.fused_attention import causal_attention, fused_attention, precompute_rope_tables
 from tinker_b200.kernels.gemm import linear, linear_rope
+from tinker_b200.kernels.kv_cache import kv_append, kv_attention
+
+# Query rows per kv head (groups * new tokens) above which a prompt at position 0 runs on the
+# tensor-core attention kernel before its keys/values are appended to the cache; below it the
+# single kv_attention launch (rotate, append, attend) is cheaper.
+PROMPT_MIN_ROWS = 64
 
 
 class TinKerAttention(nn.Module):
@@ -67,8 +73,17 @@ class TinKerAttention(nn.Module):
         self.sin_table = sin.to(device=dev)
         return self
 
-    def forward(self, x: torch.Tensor, start_pos: int = 0, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """forward pass; with ``residual`` the o_proj epilogue adds it to the output."""
+    def forward(self, x: torch.Tensor, start_pos: int = 0, residual: torch.Tensor | None = None,
+                kv_cache=None, position: torch.Tensor | None = None) -> torch.Tensor:
+        """forward pass; with ``residual`` the o_proj epilogue adds it to the output.
+
+        ``kv_cache`` (a ``KVCacheLayer``): x holds the tokens at positions ``start_pos ..`` (or from
+        the device int32 ``position[0]`` on), which attend to the cached positions before them and
+        are appended to the cache."""
+        if kv_cache is not None:
+            a = self.cached_attention(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, kv_cache,
+                                      start_pos, position)
+            return linear(a, self.o_proj.weight, residual=residual)
         hq = self.num_heads * self.head_dim
         hkv = self.num_kv_heads * self.head_dim
         if (x.dim() == 3 and self.cos_table.dtype == torch.float32 and self.sin_table.dtype == torch.float32
@@ -90,6 +105,36 @@ class TinKerAttention(nn.Module):
             start_pos=start_pos,
         )
         return linear(attn_out, self.o_proj.weight, residual=residual)
+
+    def cached_attention(self, x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, kv_cache,
+                         start_pos: int = 0, position: torch.Tensor | None = None,
+                         row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
+        """q|k|v projection of x with the weights given (the module's own, or copies with an
+        RMSNorm folded in, ``row_ssq_in``) and attention against ``kv_cache``, which receives the
+        new keys and values. Returns the attention output [B, S, num_heads * head_dim].
+
+        A prompt at position 0 with more than ``PROMPT_MIN_ROWS`` query rows per kv head takes the
+        tensor-core path (RoPE in the projection epilogue, causal attention, cache append);
+        everything else, decode steps included, one ``kv_attention`` kernel."""
+        if (x.dim() != 3 or self.cos_table.dtype != torch.float32 or self.sin_table.dtype != torch.float32
+                or self.head_dim not in (64, 128)):
+            raise ValueError("KV-cache attention needs x [batch, seq, hidden], float32 RoPE tables and "
+                             "head_dim 64 or 128")
+        B, S, _ = x.shape
+        hq = self.num_heads * self.head_dim
+        hkv = self.num_kv_heads * self.head_dim
+        groups = self.num_heads // self.num_kv_heads
+        norm = {} if row_ssq_in is None else {"row_ssq_in": row_ssq_in, "row_ssq_eps": row_ssq_eps}
+        if position is None and int(start_pos) == 0 and groups * S > PROMPT_MIN_ROWS:
+            qkv = linear_rope(x, wq, wk, wv, self.cos_table, self.sin_table, self.head_dim, 0, **norm)
+            k, v = qkv[..., hq:hq + hkv], qkv[..., hq + hkv:]
+            a = causal_attention(qkv[..., :hq], k, v, self.num_heads, self.num_kv_heads, self.head_dim)
+            kv_append(k, v, kv_cache.k, kv_cache.v, 0)
+            return a
+        qkv = linear(x, wq, wk, wv, **norm)
+        return kv_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], self.cos_table,
+                            self.sin_table, kv_cache.k, kv_cache.v, self.num_heads, self.num_kv_heads,
+                            self.head_dim, start_pos, position, kv_cache.workspace(S))
 
     @classmethod
     def from_module(
