@@ -1,4 +1,5 @@
-"""tcgen05 GEMM parity (through the C ABI) against float64 numpy.
+"""GEMM parity (through the C ABI) against float64 numpy: the tcgen05 kernels, and the
+weight-streaming kernel the same entry points use for at most 8 rows.
 
 y = x . w^T with fp32 accumulation and one rounding: the result must match the
 exactly computed product of the same half-precision inputs to within the
@@ -35,6 +36,9 @@ SHAPES = [
     (4096, 896, 896),    # large m (Qwen-shaped o_proj, 8 sequences of 512)
     (1000, 4864, 896),   # many tiles, ragged m
     (384, 2048, 5632),   # 1B down_proj, deep k
+    (3, 1536, 1024),     # decode rows: the weight-streaming path (m <= 8)
+    (8, 1024, 2816),
+    (5, 96, 40),
 ]
 
 
@@ -56,7 +60,7 @@ def test_linear(dt, m, n, k):
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
 @pytest.mark.parametrize("hq, hkv", [(1024, 256), (896, 128), (512, 512), (512, 64)])
-@pytest.mark.parametrize("m", [128, 1030])
+@pytest.mark.parametrize("m", [2, 8, 128, 1030])
 def test_linear_three_weight_blocks(dt, hq, hkv, m):
     """q|k|v projection as one GEMM over three separate weights."""
     require_b200()
@@ -74,20 +78,22 @@ def test_linear_three_weight_blocks(dt, hq, hkv, m):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-def test_linear_residual_epilogue(dt):
+@pytest.mark.parametrize("m", [300, 4])
+def test_linear_residual_epilogue(dt, m):
     require_b200()
     from tinker_b200.kernels import linear
     dtype = DTYPES[dt]
     torch.manual_seed(1)
-    x = torch.randn(300, 2816, device="cuda").to(dtype)
+    x = torch.randn(m, 2816, device="cuda").to(dtype)
     w = (0.02 * torch.randn(1024, 2816, device="cuda")).to(dtype)
-    r = torch.randn(300, 1024, device="cuda").to(dtype)
+    r = torch.randn(m, 1024, device="cuda").to(dtype)
     y = linear(x, w, residual=r)
     assert rel_err(np32(y), _ref(x, [w], r)) <= TOL[dtype]
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
 @pytest.mark.parametrize("m, hidden, f", [(128, 1024, 2816), (4096, 2048, 5632), (77, 896, 4864), (1, 512, 1376),
+                                          (8, 1024, 2816), (3, 896, 4864),
                                           (640, 256, 40)])
 def test_gate_up_swiglu(dt, m, hidden, f):
     require_b200()
@@ -176,7 +182,8 @@ def _rms_ref(x, w_norm, eps):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 5632, 1024), (300, 896, 896), (4096, 1152, 896)])
+@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 5632, 1024), (300, 896, 896), (4096, 1152, 896),
+                                     (1, 1024, 1024), (8, 1536, 1024)])
 def test_row_sumsq_and_folded_norm_linear(dt, m, n, k):
     """row_sumsq gives the per-32-column sums of squares; linear with row_ssq_in and the norm weight
     folded into w equals rmsnorm(x) @ w.T (tinker/modules/normalization.py:29-31 then nn.Linear)."""
@@ -198,7 +205,8 @@ def test_row_sumsq_and_folded_norm_linear(dt, m, n, k):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 1024, 2816), (1000, 896, 4864), (130, 96, 64)])
+@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 1024, 2816), (1000, 896, 4864), (130, 96, 64),
+                                     (1, 1024, 1024), (4, 1024, 2816), (7, 96, 64)])
 def test_row_ssq_out_of_residual_linear(dt, m, n, k):
     """row_ssq_out holds, per 32 output columns, the sum of squares of the stored (rounded) rows."""
     require_b200()
@@ -218,7 +226,8 @@ def test_row_ssq_out_of_residual_linear(dt, m, n, k):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-@pytest.mark.parametrize("m, hidden, f", [(128, 1024, 2816), (4096, 896, 4864), (256, 512, 1376)])
+@pytest.mark.parametrize("m, hidden, f", [(128, 1024, 2816), (4096, 896, 4864), (256, 512, 1376), (1, 1024, 2816),
+                                          (6, 896, 4864)])
 def test_folded_norm_gate_up_swiglu(dt, m, hidden, f):
     require_b200()
     from tinker_b200.kernels import gate_up_swiglu, row_sumsq

@@ -102,33 +102,6 @@ __device__ __forceinline__ void load_cs4(const void* t, int dt, int64_t off, flo
   }
 }
 
-// 2^x with the MUFU.EX2 approximation (PTX ex2.approx.ftz.f32; 2^-inf = +0). The
-// probabilities are rounded to 16 bits right after, far coarser than its error.
-__device__ __forceinline__ float exp2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // RoPE of one row of a swizzled [128 x D] tile, in 64-column blocks: the 32 cos and
 // 32 sin values of a block are loaded first (all in flight at once), then the
 // block's 8 chunks of the row are rotated in place in fp32 and rounded back.

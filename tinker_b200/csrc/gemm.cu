@@ -1101,6 +1101,12 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
   const int64_t n = n0 + n1 + n2;
+  if (m <= gemv::MAX_M && ex.rope_cols == 0) {  // a few rows: stream the weights once (gemv.cu)
+    const void* w[3] = {w0, n1 ? w1 : nullptr, n2 ? w2 : nullptr};
+    const int64_t nr[3] = {n0, n1, n2};
+    return gemv::run(DT, x, lda, w, nr, false, y, ldy, m, n, k, ex.residual, ex.ssq_in, ex.ssq_parts, ex.ssq_inv_k,
+                     ex.ssq_eps, ex.ssq_out, st);
+  }
   const int64_t m_tiles = (m + BM - 1) / BM;
   // all but the last weight block must be whole tiles
   const int64_t constraint = (n1 || n2) ? std::gcd(n0, n1 ? n1 : n0) : 256;
@@ -1177,6 +1183,12 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
                 int64_t f, cudaStream_t st, const Extras& ex) {
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
+  if (m <= gemv::MAX_M) {  // a few rows: stream the weights once (gemv.cu)
+    const void* w[3] = {wg, wu, nullptr};
+    const int64_t nr[3] = {f, f, 0};
+    return gemv::run(DT, x, lda, w, nr, true, h, f, m, f, hidden, nullptr, ex.ssq_in, ex.ssq_parts, ex.ssq_inv_k,
+                     ex.ssq_eps, nullptr, st);
+  }
   const int64_t m_tiles = (m + BM - 1) / BM;
   // BN counts gate + up rows; each tile produces BN/2 columns of h
   static const int cands_half[] = {128, 64, 32, 16};

@@ -15,12 +15,14 @@
 //   * the append of the new rotated k rows and v rows to the cache (row block 0 only; no
 //     other CTA of the launch reads those cache rows, they take them from the inputs);
 //   * flash-decoding over a contiguous key range: the rows of a CTA are the query rows of
-//     the `groups` query heads that share its kv head, so a key/value tile in shared memory
-//     serves all of them; two keys per lane for q.k, running max/sum per row, p.V with the
-//     lane owning D/32 output columns;
-//   * the split-K combine: each CTA stores (max, sum, unnormalised O) of its rows, the last
-//     CTA of a (sequence, kv head, row block) to arrive (atomic counter, reset by that CTA)
-//     merges them. No CTA waits for another.
+//     the `groups` query heads that share its kv head (up to 8, in every warp's registers),
+//     so each cached key is converted once for all of them. The 4 warps take interleaved
+//     32-key tiles, each with its own cp.async pipeline (2-3 stages) into shared memory;
+//     q.k with one key per lane, p.V with the lane owning D/32 output columns, both in
+//     packed fp32 FMAs; the warps' (max, sum, O) rows are merged in shared memory;
+//   * the split-K combine across CTAs: each stores (max, sum, unnormalised O) of its rows,
+//     the last CTA of a (sequence, kv head, row block) to arrive (atomic counter, reset by
+//     that CTA) merges them. No CTA waits for another.
 // The position may come from device memory (`start_dev`), so one CUDA graph serves every
 // decode step; an out-of-range position records TK_DEVERR_POSITION and leaves `out` as is.
 // The work is memory-bound (2 * kv_len * D * 2 bytes per kv head and sequence against
@@ -35,9 +37,10 @@
 namespace tk {
 namespace kvattn {
 
-constexpr int THREADS = 128;
-constexpr int WARPS = THREADS / 32;
-constexpr int KT = 64;  // keys per shared-memory tile (two per lane)
+constexpr int WARPS = 4;
+constexpr int THREADS = WARPS * 32;
+constexpr int KT = 32;                   // keys per warp tile, one per lane
+constexpr int MIN_CHUNK = WARPS * KT;    // keys per CTA at the finest split
 
 struct Params {
   const void* q;  // [batch * seq, ...] rows, head h at column h * D (no RoPE yet)
@@ -133,28 +136,55 @@ __device__ __forceinline__ void store_out(void* dst, const float* v) {
   }
 }
 
-template <int DT, int D, int RPW>
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared memory of one CTA: per warp and stage a tile of KT keys (k rows padded by 16 bytes, so
+// that the lane-per-key 128-bit reads of a quarter warp fall in distinct banks; v rows dense),
+// the CTA's q rows in fp32 and each warp's probabilities. After the key loop the ring holds the
+// warps' (max, sum) and O rows for the merge.
+template <int D, int R>
+struct Smem {
+  static constexpr int STAGES = D == 64 ? 3 : 2;
+  static constexpr int K_ROW = 2 * D + 16;
+  static constexpr int V_ROW = 2 * D;
+  static constexpr int K_TILE = KT * K_ROW;
+  static constexpr int STAGE = K_TILE + KT * V_ROW;
+  static constexpr int RING = STAGES * WARPS * STAGE;
+  static constexpr int Q_OFF = RING;                   // float [R][D], pre-scaled by log2(e)/sqrt(D)
+  static constexpr int P_OFF = Q_OFF + R * D * 4;      // float [WARPS][R][KT]
+  static constexpr int FLAG_OFF = P_OFF + WARPS * R * KT * 4;
+  static constexpr int TOTAL = FLAG_OFF + 16;
+  static constexpr int ML_BYTES = WARPS * R * 8;       // merge: float2 [WARPS][R] at the ring's start
+  static_assert(ML_BYTES % 16 == 0 || R == 1, "merge O rows must stay 16-byte aligned");
+  static_assert(32 + WARPS * R * D * 4 + ML_BYTES <= RING, "the merge buffers must fit in the ring");
+};
+
+template <int DT, int D, int R>
 __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
+  using S = Smem<D, R>;
   using T = typename Dt<DT>::T;
-  constexpr int R = WARPS * RPW;  // query rows per CTA; warp w owns rows w, w + WARPS, ...
-  constexpr int C8 = D / 8;       // 16-byte chunks per row
-  constexpr int KW = D / 2 + 1;   // padded k row in words: lanes reading different keys hit different banks
-  constexpr int VW = D / 2;
-  constexpr int DL = D / 32;      // output columns per lane
-  __shared__ __align__(16) float q_s[R][D];
-  __shared__ uint32_t k_s[KT][KW];
-  __shared__ __align__(16) uint32_t v_s[KT][VW];
-  __shared__ __align__(16) float p_s[R][KT];
-  __shared__ int last_s;
+  constexpr int C16 = D / 8;  // 16-byte chunks per row
+  constexpr int DL = D / 32;  // output columns per lane (2 or 4)
+  constexpr int HALF = D / 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* q_s = reinterpret_cast<float*>(smem + S::Q_OFF);
+  float* p_s = reinterpret_cast<float*>(smem + S::P_OFF);
+  int* last_s = reinterpret_cast<int*>(smem + S::FLAG_OFF);
 
   const int chunk = blockIdx.x;
   const int kvh = blockIdx.y / p.n_rb;
   const int rb = blockIdx.y % p.n_rb;
   const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int HALF = D / 2;
 
-  pdl_wait();  // q/k/v come from the previous kernel; the position may be written by a copy before it
+  pdl_wait();  // q/k/v come from the previous kernel; the position may be written just before
   const int start = p.start_dev ? *p.start_dev : p.start_pos;
   const int64_t end = static_cast<int64_t>(start) + p.seq;
   if (start < 0 || end > p.cap || end > p.table_rows) {
@@ -165,212 +195,267 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
   const int kv_len = static_cast<int>(end);
   const int n_tiles = (kv_len + KT - 1) / KT;
   const int per = (n_tiles + p.n_chunks - 1) / p.n_chunks;  // tiles per chunk
-  const int lo = chunk * per * KT;
-  const int hi = min(kv_len, lo + per * KT);
+  const int t_lo = chunk * per;
+  const int t_hi = min(n_tiles, t_lo + per);
+  const int hi = min(kv_len, t_hi * KT);
+  const int cached_hi = min(hi, start);  // keys below this come from the cache
   const int64_t cache_row0 = (static_cast<int64_t>(b) * p.num_kv_heads + kvh) * p.cap;
-  const T* kc_in = reinterpret_cast<const T*>(p.kc);
-  const T* vc_in = reinterpret_cast<const T*>(p.vc);
+  const T* kc = reinterpret_cast<const T*>(p.kc);
+  const T* vc = reinterpret_cast<const T*>(p.vc);
+  const uint32_t ring = smem_u32(smem);
 
-  float m[RPW], l[RPW], o[RPW][DL];
-  int qpos[RPW];
+  // this warp's tiles: t_lo + warp, t_lo + warp + WARPS, ...
+  const int first = t_lo + warp;
+  const int n_my = first < t_hi ? (t_hi - first + WARPS - 1) / WARPS : 0;
+  auto issue = [&](int i) {  // cp.async of the warp's i-th tile into stage i % STAGES
+    const int t = first + WARPS * i;
+    const uint32_t kb = ring + ((i % S::STAGES) * WARPS + warp) * S::STAGE;
+    const uint32_t vb = kb + S::K_TILE;
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int gr = rb * R + warp + WARPS * i;
-    qpos[i] = gr < p.rows ? start + gr / p.groups : -1;  // -1: padding row, every key masked
-    m[i] = -INFINITY;
-    l[i] = 0.f;
+    for (int j = 0; j < C16; ++j) {
+      const int idx = lane + 32 * j;
+      const int row = idx / C16, c = idx % C16;
+      const int kp = t * KT + row;
+      const bool cached = kp < cached_hi;  // new keys are written in after the copy, the rest is zero
+      const int64_t off = (cache_row0 + (cached ? kp : 0)) * D + c * 8;
+      cp_async16(kb + row * S::K_ROW + c * 16, kc + off, cached ? 16u : 0u);
+      cp_async16(vb + row * S::V_ROW + c * 16, vc + off, cached ? 16u : 0u);
+    }
+  };
 #pragma unroll
-    for (int d = 0; d < DL; ++d) o[i][d] = 0.f;
+  for (int i = 0; i < S::STAGES - 1; ++i) {
+    if (i < n_my) issue(i);
+    cp_async_commit();
   }
 
-  if (lo < hi) {
-    // q rows: RoPE at their positions, rounded to DT, times log2(e)/sqrt(D)
-    for (int idx = threadIdx.x; idx < R * C8; idx += THREADS) {
-      const int lr = idx / C8, c = idx % C8;
-      const int gr = rb * R + lr;
-      float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (gr < p.rows) {
-        const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
-        load8<DT>(p.q, (static_cast<int64_t>(b) * p.seq + s) * p.qs + static_cast<int64_t>(h) * D + c * 8, f);
-        (void)rope8<DT>(f, p, start + s, c * 4, HALF);
+  // q rows of the CTA: RoPE at their positions, rounded to DT, times log2(e)/sqrt(D)
+  for (int idx = threadIdx.x; idx < R * C16; idx += THREADS) {
+    const int lr = idx / C16, c = idx % C16;
+    const int gr = rb * R + lr;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (gr < p.rows) {
+      const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
+      load8<DT>(p.q, (static_cast<int64_t>(b) * p.seq + s) * p.qs + static_cast<int64_t>(h) * D + c * 8, f);
+      (void)rope8<DT>(f, p, start + s, c * 4, HALF);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] *= p.scale_log2;
-      }
-      float4* dst = reinterpret_cast<float4*>(&q_s[lr][c * 8]);
-      dst[0] = make_float4(f[0], f[1], f[2], f[3]);
-      dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+      for (int j = 0; j < 8; ++j) f[j] *= p.scale_log2;
     }
+    float4* dst = reinterpret_cast<float4*>(q_s + lr * D + c * 8);
+    dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+    dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+  __syncthreads();
 
-    for (int t0 = lo; t0 < hi; t0 += KT) {
-      __syncthreads();  // q_s written; the previous tile's k_s / v_s / p_s reads are done
-      for (int idx = threadIdx.x; idx < KT * C8; idx += THREADS) {
-        const int key = idx / C8, c = idx % C8;
-        const int kp = t0 + key;
-        uint4 kw = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
-        if (kp < hi) {
+  float m[R], l[R];
+  uint64_t o2[R][DL / 2];  // O columns lane*DL .. lane*DL+DL-1 as packed pairs
+  int qpos[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int gr = rb * R + r;
+    qpos[r] = gr < p.rows ? start + gr / p.groups : -1;  // -1: padding row, every key masked
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL / 2; ++d) o2[r][d] = 0ull;
+  }
+  float* pw = p_s + warp * R * KT;
+
+  for (int i = 0; i < n_my; ++i) {
+    if (i + S::STAGES - 1 < n_my) issue(i + S::STAGES - 1);
+    cp_async_commit();
+    cp_async_wait<S::STAGES - 1>();
+    __syncwarp();  // every lane's copies of tile i have landed
+    const int t0 = (first + WARPS * i) * KT;
+    uint8_t* kbuf = smem + ((i % S::STAGES) * WARPS + warp) * S::STAGE;
+    uint8_t* vbuf = kbuf + S::K_TILE;
+    if (t0 + KT > start && t0 < hi) {
+      // the tile holds new keys: rotate them in (and append them to the cache, row block 0)
+      const int r0 = max(t0, start), n_new = min(t0 + KT, hi) - r0;
+      for (int idx = lane; idx < n_new * C16; idx += 32) {
+        const int kp = r0 + idx / C16, c = idx % C16;
+        const int64_t trow = static_cast<int64_t>(b) * p.seq + (kp - start);
+        float f[8];
+        load8<DT>(p.k, trow * p.ks + static_cast<int64_t>(kvh) * D + c * 8, f);
+        const uint4 kw = rope8<DT>(f, p, kp, c * 4, HALF);
+        const uint4 vw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + trow * p.vs +
+                                                         static_cast<int64_t>(kvh) * D + c * 8);
+        *reinterpret_cast<uint4*>(kbuf + (kp - t0) * S::K_ROW + c * 16) = kw;
+        *reinterpret_cast<uint4*>(vbuf + (kp - t0) * S::V_ROW + c * 16) = vw;
+        if (rb == 0) {
           const int64_t crow = (cache_row0 + kp) * D + c * 8;
-          if (kp < start) {
-            kw = *reinterpret_cast<const uint4*>(kc_in + crow);
-            vw = *reinterpret_cast<const uint4*>(vc_in + crow);
-          } else {
-            const int64_t trow = static_cast<int64_t>(b) * p.seq + (kp - start);
-            float f[8];
-            load8<DT>(p.k, trow * p.ks + static_cast<int64_t>(kvh) * D + c * 8, f);
-            kw = rope8<DT>(f, p, kp, c * 4, HALF);
-            vw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + trow * p.vs +
-                                                 static_cast<int64_t>(kvh) * D + c * 8);
-            if (rb == 0) {
-              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.kc) + crow) = kw;
-              *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.vc) + crow) = vw;
-            }
-          }
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.kc) + crow) = kw;
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.vc) + crow) = vw;
         }
-        uint32_t* kd = &k_s[key][c * 4];
-        kd[0] = kw.x;
-        kd[1] = kw.y;
-        kd[2] = kw.z;
-        kd[3] = kw.w;
-        *reinterpret_cast<uint4*>(&v_s[key][c * 4]) = vw;
-      }
-      __syncthreads();
-
-      // scores of keys t0 + lane and t0 + lane + 32 for each of the warp's rows
-      float sc[RPW][2];
-#pragma unroll
-      for (int i = 0; i < RPW; ++i) sc[i][0] = sc[i][1] = 0.f;
-#pragma unroll 4
-      for (int w2 = 0; w2 < D / 4; ++w2) {
-        const float2 a0 = unpack_word<DT>(k_s[lane][2 * w2]);
-        const float2 a1 = unpack_word<DT>(k_s[lane][2 * w2 + 1]);
-        const float2 b0 = unpack_word<DT>(k_s[lane + 32][2 * w2]);
-        const float2 b1 = unpack_word<DT>(k_s[lane + 32][2 * w2 + 1]);
-#pragma unroll
-        for (int i = 0; i < RPW; ++i) {
-          const float4 qv = *reinterpret_cast<const float4*>(&q_s[warp + WARPS * i][4 * w2]);
-          sc[i][0] = fmaf(qv.x, a0.x, fmaf(qv.y, a0.y, fmaf(qv.z, a1.x, fmaf(qv.w, a1.y, sc[i][0]))));
-          sc[i][1] = fmaf(qv.x, b0.x, fmaf(qv.y, b0.y, fmaf(qv.z, b1.x, fmaf(qv.w, b1.y, sc[i][1]))));
-        }
-      }
-      const int kp0 = t0 + lane, kp1 = t0 + lane + 32;
-#pragma unroll
-      for (int i = 0; i < RPW; ++i) {
-        const float s0 = (kp0 < hi && kp0 <= qpos[i]) ? sc[i][0] : -INFINITY;
-        const float s1 = (kp1 < hi && kp1 <= qpos[i]) ? sc[i][1] : -INFINITY;
-        const float mn = fmaxf(m[i], warp_max(fmaxf(s0, s1)));
-        float p0 = 0.f, p1 = 0.f, alpha = 1.f;
-        if (mn != -INFINITY) {  // some key of this row seen so far
-          alpha = exp2f(m[i] - mn);
-          p0 = exp2f(s0 - mn);
-          p1 = exp2f(s1 - mn);
-        }
-        m[i] = mn;
-        l[i] = l[i] * alpha + (p0 + p1);  // per-lane partial sum, reduced at the end
-#pragma unroll
-        for (int d = 0; d < DL; ++d) o[i][d] *= alpha;
-        p_s[warp + WARPS * i][lane] = p0;
-        p_s[warp + WARPS * i][lane + 32] = p1;
       }
       __syncwarp();
+    }
 
-      // O += P V over the tile's keys (the lane's DL columns)
-      const int kn = min(KT, hi - t0);
-      for (int k4 = 0; k4 < kn; k4 += 4) {
-        float4 pv[RPW];
+    // score of key t0 + lane for every row: two packed accumulators per row
+    uint64_t acc[R][2];
 #pragma unroll
-        for (int i = 0; i < RPW; ++i) pv[i] = *reinterpret_cast<const float4*>(&p_s[warp + WARPS * i][k4]);
+    for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = 0ull;
+    const uint8_t* krow = kbuf + lane * S::K_ROW;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          float vv[DL];
-          if constexpr (DL == 2) {
-            const float2 t = unpack_word<DT>(v_s[k4 + kk][lane]);
-            vv[0] = t.x;
-            vv[1] = t.y;
-          } else {
-            const uint2 w = *reinterpret_cast<const uint2*>(&v_s[k4 + kk][2 * lane]);
-            const float2 t0v = unpack_word<DT>(w.x), t1v = unpack_word<DT>(w.y);
-            vv[0] = t0v.x;
-            vv[1] = t0v.y;
-            vv[2] = t1v.x;
-            vv[3] = t1v.y;
-          }
+    for (int j = 0; j < C16; ++j) {
+      const uint4 kw = *reinterpret_cast<const uint4*>(krow + j * 16);
+      const float2 k0 = unpack_word<DT>(kw.x), k1 = unpack_word<DT>(kw.y);
+      const float2 k2 = unpack_word<DT>(kw.z), k3 = unpack_word<DT>(kw.w);
+      const uint64_t kk0 = pack_f32x2(k0.x, k0.y), kk1 = pack_f32x2(k1.x, k1.y);
+      const uint64_t kk2 = pack_f32x2(k2.x, k2.y), kk3 = pack_f32x2(k3.x, k3.y);
 #pragma unroll
-          for (int i = 0; i < RPW; ++i) {
-            const float pk = kk == 0 ? pv[i].x : kk == 1 ? pv[i].y : kk == 2 ? pv[i].z : pv[i].w;
+      for (int r = 0; r < R; ++r) {
+        const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q_s + r * D + 8 * j);
+        const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q_s + r * D + 8 * j + 4);
+        acc[r][0] = fma_f32x2(qa.x, kk0, acc[r][0]);
+        acc[r][1] = fma_f32x2(qa.y, kk1, acc[r][1]);
+        acc[r][0] = fma_f32x2(qb.x, kk2, acc[r][0]);
+        acc[r][1] = fma_f32x2(qb.y, kk3, acc[r][1]);
+      }
+    }
+    const int kp = t0 + lane;
 #pragma unroll
-            for (int d = 0; d < DL; ++d) o[i][d] = fmaf(pk, vv[d], o[i][d]);
-          }
+    for (int r = 0; r < R; ++r) {
+      float a0, a1, b0, b1;
+      unpack_f32x2(acc[r][0], a0, a1);
+      unpack_f32x2(acc[r][1], b0, b1);
+      const float sr = (kp < hi && kp <= qpos[r]) ? (a0 + a1) + (b0 + b1) : -INFINITY;
+      const float mn = fmaxf(m[r], warp_max(sr));
+      float pr = 0.f;
+      if (mn != -INFINITY) {  // warp-uniform: some key of this row seen so far
+        pr = exp2_approx(sr - mn);
+        if (mn != m[r]) {
+          const float alpha = exp2_approx(m[r] - mn);
+          const uint64_t a2 = pack_f32x2(alpha, alpha);
+          l[r] *= alpha;
+#pragma unroll
+          for (int d = 0; d < DL / 2; ++d) o2[r][d] = fma_f32x2(o2[r][d], a2, 0ull);
+        }
+        m[r] = mn;
+      }
+      l[r] += pr;  // per-lane partial sum, reduced after the loop
+      pw[r * KT + lane] = pr;
+    }
+    __syncwarp();
+
+    // O += P V over the tile's keys
+#pragma unroll 2
+    for (int k = 0; k < KT; k += 4) {
+      float4 p4[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) p4[r] = *reinterpret_cast<const float4*>(pw + r * KT + k);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint64_t vv[DL / 2];
+        if constexpr (DL == 2) {
+          const float2 v = unpack_word<DT>(*reinterpret_cast<const uint32_t*>(vbuf + (k + kk) * S::V_ROW + lane * 4));
+          vv[0] = pack_f32x2(v.x, v.y);
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(vbuf + (k + kk) * S::V_ROW + lane * 8);
+          const float2 v0 = unpack_word<DT>(w.x), v1 = unpack_word<DT>(w.y);
+          vv[0] = pack_f32x2(v0.x, v0.y);
+          vv[1] = pack_f32x2(v1.x, v1.y);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float pk = kk == 0 ? p4[r].x : kk == 1 ? p4[r].y : kk == 2 ? p4[r].z : p4[r].w;
+          const uint64_t pp = pack_f32x2(pk, pk);
+#pragma unroll
+          for (int d = 0; d < DL / 2; ++d) o2[r][d] = fma_f32x2(pp, vv[d], o2[r][d]);
         }
       }
     }
+    __syncwarp();  // the stage and pw are rewritten by the next iterations
   }
+  cp_async_wait<0>();
   pdl_launch_dependents();
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) l[i] = warp_sum(l[i]);
+  for (int r = 0; r < R; ++r) l[r] = warp_sum(l[r]);
 
-  if (p.n_chunks == 1) {  // the only chunk: normalise and store
+  // merge the warps' rows in shared memory (the ring is free now)
+  __syncthreads();
+  float2* ml_s = reinterpret_cast<float2*>(smem);                 // [WARPS][R]
+  float* o_s = reinterpret_cast<float*>(smem + (S::ML_BYTES + 15) / 16 * 16);  // [WARPS][R][D]
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      if (qpos[i] < 0) continue;
-      const int gr = rb * R + warp + WARPS * i;
-      const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
-      const float inv = 1.f / l[i];
-      float v[DL];
-#pragma unroll
-      for (int d = 0; d < DL; ++d) v[d] = o[i][d] * inv;
-      T* dst = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.seq + s) * p.os +
-               static_cast<int64_t>(h) * D + lane * DL;
-      store_out<DT, DL>(dst, v);
+  for (int r = 0; r < R; ++r) {
+    if (lane == 0) ml_s[warp * R + r] = make_float2(m[r], l[r]);
+    float* dst = o_s + (warp * R + r) * D + lane * DL;
+    if constexpr (DL == 2) {
+      *reinterpret_cast<uint64_t*>(dst) = o2[r][0];
+    } else {
+      *reinterpret_cast<ulonglong2*>(dst) = make_ulonglong2(o2[r][0], o2[r][1]);
     }
-    return;
   }
+  __syncthreads();
 
   const int unit = b * gridDim.y + blockIdx.y;
+  constexpr int D4 = D / 4;
+  for (int idx = threadIdx.x; idx < R * D4; idx += THREADS) {
+    const int r = idx / D4, d = (idx % D4) * 4;
+    const int gr = rb * R + r;
+    if (gr >= p.rows) continue;
+    float M = -INFINITY, L = 0.f;
+    float acc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int64_t slot = (static_cast<int64_t>(unit) * p.n_chunks + chunk) * R + warp + WARPS * i;
-    if (lane == 0) p.part_ml[slot] = make_float2(m[i], l[i]);
-    float* dst = p.part_o + slot * D + lane * DL;
-    if constexpr (DL == 2) {
-      *reinterpret_cast<float2*>(dst) = make_float2(o[i][0], o[i][1]);
+    for (int w = 0; w < WARPS; ++w) {
+      const float2 ml = ml_s[w * R + r];
+      if (ml.y == 0.f) continue;  // no key of this row in warp w's tiles
+      const float4 ov = *reinterpret_cast<const float4*>(o_s + (w * R + r) * D + d);
+      const float mn = fmaxf(M, ml.x);
+      const float a = exp2_approx(M - mn), e = exp2_approx(ml.x - mn);
+      L = L * a + ml.y * e;
+      acc4[0] = acc4[0] * a + ov.x * e;
+      acc4[1] = acc4[1] * a + ov.y * e;
+      acc4[2] = acc4[2] * a + ov.z * e;
+      acc4[3] = acc4[3] * a + ov.w * e;
+      M = mn;
+    }
+    if (p.n_chunks == 1) {  // the only chunk: normalise and store
+      const float inv = 1.f / L;
+      float v[4] = {acc4[0] * inv, acc4[1] * inv, acc4[2] * inv, acc4[3] * inv};
+      const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
+      store_out<DT, 4>(reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.seq + s) * p.os +
+                           static_cast<int64_t>(h) * D + d, v);
     } else {
-      *reinterpret_cast<float4*>(dst) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+      const int64_t slot = (static_cast<int64_t>(unit) * p.n_chunks + chunk) * R + r;
+      if (d == 0) p.part_ml[slot] = make_float2(M, L);
+      *reinterpret_cast<float4*>(p.part_o + slot * D + d) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
     }
   }
+  if (p.n_chunks == 1) return;
+
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_s = atomicAdd(p.counters + unit, 1) == p.n_chunks - 1;
+  if (threadIdx.x == 0) *last_s = atomicAdd(p.counters + unit, 1) == p.n_chunks - 1;
   __syncthreads();
-  if (!last_s) return;
+  if (!*last_s) return;
   __threadfence();
 
   // last CTA of this unit: merge the chunks' partial rows
-  constexpr int D4 = D / 4;
   for (int idx = threadIdx.x; idx < R * D4; idx += THREADS) {
-    const int lr = idx / D4, d = (idx % D4) * 4;
-    const int gr = rb * R + lr;
+    const int r = idx / D4, d = (idx % D4) * 4;
+    const int gr = rb * R + r;
     if (gr >= p.rows) continue;
     float M = -INFINITY, L = 0.f;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc4[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = 0; c < p.n_chunks; ++c) {
-      const int64_t slot = (static_cast<int64_t>(unit) * p.n_chunks + c) * R + lr;
+      const int64_t slot = (static_cast<int64_t>(unit) * p.n_chunks + c) * R + r;
       const float2 ml = __ldcg(p.part_ml + slot);
       if (ml.y == 0.f) continue;  // no key of this row in chunk c
       const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.part_o + slot * D + d));
       const float mn = fmaxf(M, ml.x);
-      const float a = exp2f(M - mn), w = exp2f(ml.x - mn);
-      L = L * a + ml.y * w;
-      acc[0] = acc[0] * a + ov.x * w;
-      acc[1] = acc[1] * a + ov.y * w;
-      acc[2] = acc[2] * a + ov.z * w;
-      acc[3] = acc[3] * a + ov.w * w;
+      const float a = exp2_approx(M - mn), e = exp2_approx(ml.x - mn);
+      L = L * a + ml.y * e;
+      acc4[0] = acc4[0] * a + ov.x * e;
+      acc4[1] = acc4[1] * a + ov.y * e;
+      acc4[2] = acc4[2] * a + ov.z * e;
+      acc4[3] = acc4[3] * a + ov.w * e;
       M = mn;
     }
     const float inv = 1.f / L;
-    float v[4] = {acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv};
+    float v[4] = {acc4[0] * inv, acc4[1] * inv, acc4[2] * inv, acc4[3] * inv};
     const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
-    T* dst = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.seq + s) * p.os +
-             static_cast<int64_t>(h) * D + d;
-    store_out<DT, 4>(dst, v);
+    store_out<DT, 4>(reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.seq + s) * p.os +
+                         static_cast<int64_t>(h) * D + d, v);
   }
   if (threadIdx.x == 0) p.counters[unit] = 0;  // ready for the next launch
 }
@@ -402,7 +487,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const void* k, int64_t k
 }
 
 struct Plan {
-  int rpw, rows_cta, n_rb, n_chunks;
+  int rows_cta, n_rb, n_chunks;
   int64_t units;
   size_t counters_bytes, ml_bytes, o_bytes;
   size_t bytes() const { return n_chunks > 1 ? counters_bytes + ml_bytes + o_bytes : 0; }
@@ -410,17 +495,18 @@ struct Plan {
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Rows per CTA, row blocks and key chunks for a launch whose key count is at most `max_kv`;
-// about two CTAs per SM unless the keys run out. The workspace a plan needs grows with max_kv.
+// Rows per CTA (1, 4 or 8: every warp holds all of them), row blocks, and key chunks for a
+// launch attending to at most `max_kv` keys: enough chunks for about 1.5 CTAs per SM, each at
+// least WARPS tiles long. n_chunks never decreases with max_kv, so the workspace sized for a
+// cache's capacity covers every position.
 Plan make_plan(int batch, int num_kv_heads, int rows, int max_kv, int head_dim, int sm_count) {
   Plan pl{};
-  pl.rpw = rows <= WARPS ? 1 : rows <= 2 * WARPS ? 2 : 4;
-  pl.rows_cta = WARPS * pl.rpw;
+  pl.rows_cta = rows == 1 ? 1 : rows <= 4 ? 4 : 8;
   pl.n_rb = (rows + pl.rows_cta - 1) / pl.rows_cta;
   pl.units = static_cast<int64_t>(batch) * num_kv_heads * pl.n_rb;
-  const int max_tiles = std::max(1, (max_kv + KT - 1) / KT);
-  const int64_t target = 2 * static_cast<int64_t>(std::max(sm_count, 1));
-  pl.n_chunks = static_cast<int>(std::min<int64_t>(max_tiles, std::max<int64_t>(1, (target + pl.units - 1) / pl.units)));
+  const int64_t max_chunks = std::max(1, (max_kv + MIN_CHUNK - 1) / MIN_CHUNK);
+  const int64_t want = (3 * static_cast<int64_t>(std::max(sm_count, 1)) / 2 + pl.units - 1) / pl.units;
+  pl.n_chunks = static_cast<int>(std::max<int64_t>(1, std::min(max_chunks, want)));
   pl.counters_bytes = round_up(static_cast<size_t>(pl.units) * sizeof(int), 256);
   const size_t slots = static_cast<size_t>(pl.units) * pl.n_chunks * pl.rows_cta;
   pl.ml_bytes = round_up(slots * sizeof(float2), 256);
@@ -439,17 +525,28 @@ int check_sizes(const char* what, int batch, int seq, int num_heads, int num_kv_
   return TK_OK;
 }
 
-template <int DT, int D, int RPW>
+template <int DT, int D, int R>
 int launch(const Params& p, dim3 grid, cudaStream_t st) {
-  return launch_kernel(kv_attention_kernel<DT, D, RPW>, grid, dim3(THREADS), 0, st, 1, "kv_attention", p);
+  using S = Smem<D, R>;
+  auto kern = kv_attention_kernel<DT, D, R>;
+  static bool configured[64] = {};
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  if (!configured[dev.device]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL),
+                            "cudaFuncSetAttribute(kv_attention)"))
+      return rc;
+    configured[dev.device] = true;
+  }
+  return launch_kernel(kern, grid, dim3(THREADS), S::TOTAL, st, 1, "kv_attention", p);
 }
 
 template <int DT, int D>
-int launch_rpw(int rpw, const Params& p, dim3 grid, cudaStream_t st) {
-  switch (rpw) {
+int launch_rows(int rows_cta, const Params& p, dim3 grid, cudaStream_t st) {
+  switch (rows_cta) {
     case 1: return launch<DT, D, 1>(p, grid, st);
-    case 2: return launch<DT, D, 2>(p, grid, st);
-    default: return launch<DT, D, 4>(p, grid, st);
+    case 4: return launch<DT, D, 4>(p, grid, st);
+    default: return launch<DT, D, 8>(p, grid, st);
   }
 }
 
@@ -539,8 +636,8 @@ extern "C" int tk_kv_attention(const void* q, int64_t q_tok_stride, const void* 
   const dim3 grid(pl.n_chunks, num_kv_heads * pl.n_rb, batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TK_F16)
-    return head_dim == 64 ? launch_rpw<TK_F16, 64>(pl.rpw, p, grid, st) : launch_rpw<TK_F16, 128>(pl.rpw, p, grid, st);
-  return head_dim == 64 ? launch_rpw<TK_BF16, 64>(pl.rpw, p, grid, st) : launch_rpw<TK_BF16, 128>(pl.rpw, p, grid, st);
+    return head_dim == 64 ? launch_rows<TK_F16, 64>(pl.rows_cta, p, grid, st) : launch_rows<TK_F16, 128>(pl.rows_cta, p, grid, st);
+  return head_dim == 64 ? launch_rows<TK_BF16, 64>(pl.rows_cta, p, grid, st) : launch_rows<TK_BF16, 128>(pl.rows_cta, p, grid, st);
 }
 
 extern "C" int tk_kv_append(const void* k, int64_t k_tok_stride, const void* v, int64_t v_tok_stride, void* k_cache,

@@ -83,4 +83,15 @@ int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, 
 int tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d0, uint64_t d1, uint64_t d2,
                   uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
 
+// Weight-streaming products for 1..MAX_M rows (gemv.cu): y = x W^T over up to three weight
+// blocks stacked along n (nrows[i] rows each, w[i] null when absent), with the GEMM epilogue
+// options, or SwiGLU of gate w[0] and up w[1] (n output columns). Used by the GEMM entry points
+// for small M.
+namespace gemv {
+constexpr int MAX_M = 8;
+int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int64_t nrows[3], bool swiglu, void* y,
+        int64_t ldy, int64_t m, int64_t n, int64_t k, const void* residual, const float* ssq_in, int ssq_parts,
+        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st);
+}  // namespace gemv
+
 }  // namespace tk
