@@ -409,10 +409,12 @@ def _decode_bench(dev, peaks, peak_note, batch: int, prompt: int = DECODE_PROMPT
         lg = dec.prefill(ids)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")  # profilers select the decode steps with an NVTX filter
         e0.record()
         for _ in range(new):
             lg = dec.decode(lg.argmax(-1))
         e1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / new
         dec.reset()

@@ -9,7 +9,8 @@
 // (CPW output columns, or CPW gate + CPW up rows for SwiGLU); its lanes take interleaved
 // 16-byte chunks of K, so a warp reads CPW * 512 contiguous bytes per step; products are
 // packed fp32 FMAs, then one butterfly reduction per (row, m). A CTA of 8 warps covers
-// 8 * CPW columns, 32 when the ssq_out partial of a 32-column chunk must come from one CTA.
+// 8 * CPW columns; with ssq_out, a cluster of CL CTAs covers one 32-column chunk and its rank
+// 0 adds the CTAs' sums of squares from distributed shared memory (fixed order).
 #include <algorithm>
 
 #include "tk_common.cuh"
@@ -54,11 +55,13 @@ __device__ __forceinline__ float row_scale(const Params& p, int row) {
 }
 
 // SWIGLU: column j needs gate row j and up row j (ROWS = 2 * CPW weight rows per warp).
-template <int DT, int M, int CPW, bool SWIGLU>
+// CL: CTAs per cluster (WARPS * CPW * CL == 32 when ssq_out is used).
+template <int DT, int M, int CPW, bool SWIGLU, int CL>
 __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
   using T = typename Dt<DT>::T;
   constexpr int ROWS = SWIGLU ? 2 * CPW : CPW;
   __shared__ float ssq_s[WARPS][M];
+  __shared__ float cta_ssq[M];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col0 = (blockIdx.x * WARPS + warp) * CPW;  // first output column of this warp
   const int kc = p.k >> 3;                              // 16-byte chunks per row
@@ -158,43 +161,57 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
       sq[m] = fmaf(rv, rv, sq[m]);
       if (lane == c * M + m) reinterpret_cast<T*>(p.y)[static_cast<int64_t>(m) * p.ldy + col] = t;
     }
-  if (!SWIGLU && p.ssq_out) {  // CTA = one 32-column chunk (CPW == 4)
+  if (!SWIGLU && p.ssq_out) {  // the CL CTAs of a cluster = one 32-column chunk
     if (lane == 0)
 #pragma unroll
       for (int m = 0; m < M; ++m) ssq_s[warp][m] = sq[m];
     __syncthreads();
-    if (threadIdx.x < p.m && threadIdx.x < M) {
+    if (threadIdx.x < M) {
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < WARPS; ++w) s += ssq_s[w][threadIdx.x];
-      p.ssq_out[static_cast<int64_t>(blockIdx.x) * p.m + threadIdx.x] = s;
+      cta_ssq[threadIdx.x] = s;
+    }
+    if constexpr (CL == 1) {
+      if (threadIdx.x < p.m && threadIdx.x < M)
+        p.ssq_out[static_cast<int64_t>(blockIdx.x) * p.m + threadIdx.x] = cta_ssq[threadIdx.x];
+    } else {
+      cluster_sync();  // every CTA's cta_ssq written
+      if (cluster_ctarank() == 0 && threadIdx.x < p.m && threadIdx.x < M) {
+        float s = 0.f;
+#pragma unroll
+        for (int r = 0; r < CL; ++r) s += ld_cluster_f32(mapa_shared(smem_u32(&cta_ssq[threadIdx.x]), r));
+        p.ssq_out[static_cast<int64_t>(blockIdx.x / CL) * p.m + threadIdx.x] = s;
+      }
+      cluster_sync();  // the peers keep their shared memory until rank 0 has read it
     }
   }
 }
 
-template <int DT, int M, int CPW, bool SWIGLU>
+template <int DT, int M, int CPW, bool SWIGLU, int CL>
 int launch_m(const Params& p, cudaStream_t st) {
   const int cols = WARPS * CPW;
-  const int grid = (p.n + cols - 1) / cols;
-  return launch_kernel(gemv_kernel<DT, M, CPW, SWIGLU>, dim3(grid), dim3(THREADS), 0, st, 1, "gemv", p);
+  const int grid = ((p.n + cols - 1) / cols + CL - 1) / CL * CL;  // whole clusters
+  return launch_kernel(gemv_kernel<DT, M, CPW, SWIGLU, CL>, dim3(grid), dim3(THREADS), 0, st, CL, "gemv", p);
 }
 
-template <int DT, int CPW, bool SWIGLU>
+template <int DT, int CPW, bool SWIGLU, int CL>
 int launch_cpw(const Params& p, cudaStream_t st) {
   switch (p.m) {
-    case 1: return launch_m<DT, 1, CPW, SWIGLU>(p, st);
-    case 2: return launch_m<DT, 2, CPW, SWIGLU>(p, st);
+    case 1: return launch_m<DT, 1, CPW, SWIGLU, CL>(p, st);
+    case 2: return launch_m<DT, 2, CPW, SWIGLU, CL>(p, st);
     case 3:
-    case 4: return launch_m<DT, 4, CPW, SWIGLU>(p, st);
-    default: return launch_m<DT, 8, CPW, SWIGLU>(p, st);
+    case 4: return launch_m<DT, 4, CPW, SWIGLU, CL>(p, st);
+    default: return launch_m<DT, 8, CPW, SWIGLU, CL>(p, st);
   }
 }
 
 template <int DT>
 int launch_dt(const Params& p, bool swiglu, int cpw, cudaStream_t st) {
-  if (swiglu) return cpw == 1 ? launch_cpw<DT, 1, true>(p, st) : launch_cpw<DT, 2, true>(p, st);
-  if (cpw == 4) return launch_cpw<DT, 4, false>(p, st);
-  return cpw == 2 ? launch_cpw<DT, 2, false>(p, st) : launch_cpw<DT, 1, false>(p, st);
+  if (swiglu) return cpw == 1 ? launch_cpw<DT, 1, true, 1>(p, st) : launch_cpw<DT, 2, true, 1>(p, st);
+  if (p.ssq_out) return launch_cpw<DT, 1, false, 4>(p, st);  // 8 columns per CTA, 4 CTAs per chunk
+  if (cpw == 4) return launch_cpw<DT, 4, false, 1>(p, st);
+  return cpw == 2 ? launch_cpw<DT, 2, false, 1>(p, st) : launch_cpw<DT, 1, false, 1>(p, st);
 }
 
 int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int64_t nrows[3], bool swiglu, void* y,
@@ -225,16 +242,11 @@ int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  // columns per warp: 4 when a CTA must cover a whole 32-column ssq chunk, else the most that
-  // still gives about two CTAs per SM
-  int cpw;
-  if (!swiglu && ssq_out) {
-    cpw = 4;
-  } else {
-    const int max_cpw = swiglu ? 2 : 4;
-    cpw = 1;
-    while (cpw < max_cpw && (n + WARPS * cpw * 2 - 1) / (WARPS * cpw * 2) >= 2 * dev.sm_count) cpw *= 2;
-  }
+  // columns per warp: the most that still gives about two CTAs per SM (one with ssq_out, whose
+  // 32-column chunks are split over clusters of 4 CTAs)
+  const int max_cpw = swiglu ? 2 : 4;
+  int cpw = 1;
+  while (cpw < max_cpw && (n + WARPS * cpw * 2 - 1) / (WARPS * cpw * 2) >= 2 * dev.sm_count) cpw *= 2;
   return dtype == TK_F16 ? launch_dt<TK_F16>(p, swiglu, cpw, st) : launch_dt<TK_BF16>(p, swiglu, cpw, st);
 }
 

@@ -40,7 +40,7 @@ namespace kvattn {
 constexpr int WARPS = 4;
 constexpr int THREADS = WARPS * 32;
 constexpr int KT = 32;                   // keys per warp tile, one per lane
-constexpr int MIN_CHUNK = WARPS * KT;    // keys per CTA at the finest split
+constexpr int CHUNK_KEYS = 256;          // keys per CTA at the finest split of the key axis
 
 struct Params {
   const void* q;  // [batch * seq, ...] rows, head h at column h * D (no RoPE yet)
@@ -193,8 +193,12 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
     return;
   }
   const int kv_len = static_cast<int>(end);
+  // chunks in use for this length (the launch covers the longest): a short context is not split,
+  // so it needs no combine; CTAs past them leave before touching memory
+  const int n_chunks = min(p.n_chunks, (kv_len + CHUNK_KEYS - 1) / CHUNK_KEYS);
+  if (chunk >= n_chunks) return;
   const int n_tiles = (kv_len + KT - 1) / KT;
-  const int per = (n_tiles + p.n_chunks - 1) / p.n_chunks;  // tiles per chunk
+  const int per = (n_tiles + n_chunks - 1) / n_chunks;  // tiles per chunk
   const int t_lo = chunk * per;
   const int t_hi = min(n_tiles, t_lo + per);
   const int hi = min(kv_len, t_hi * KT);
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
       acc4[3] = acc4[3] * a + ov.w * e;
       M = mn;
     }
-    if (p.n_chunks == 1) {  // the only chunk: normalise and store
+    if (n_chunks == 1) {  // the only chunk: normalise and store
       const float inv = 1.f / L;
       float v[4] = {acc4[0] * inv, acc4[1] * inv, acc4[2] * inv, acc4[3] * inv};
       const int s = gr / p.groups, h = kvh * p.groups + gr % p.groups;
@@ -421,11 +425,11 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
       *reinterpret_cast<float4*>(p.part_o + slot * D + d) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
     }
   }
-  if (p.n_chunks == 1) return;
+  if (n_chunks == 1) return;
 
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) *last_s = atomicAdd(p.counters + unit, 1) == p.n_chunks - 1;
+  if (threadIdx.x == 0) *last_s = atomicAdd(p.counters + unit, 1) == n_chunks - 1;
   __syncthreads();
   if (!*last_s) return;
   __threadfence();
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
     if (gr >= p.rows) continue;
     float M = -INFINITY, L = 0.f;
     float acc4[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < p.n_chunks; ++c) {
+    for (int c = 0; c < n_chunks; ++c) {
       const int64_t slot = (static_cast<int64_t>(unit) * p.n_chunks + c) * R + r;
       const float2 ml = __ldcg(p.part_ml + slot);
       if (ml.y == 0.f) continue;  // no key of this row in chunk c
@@ -497,14 +501,15 @@ inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Rows per CTA (1, 4 or 8: every warp holds all of them), row blocks, and key chunks for a
 // launch attending to at most `max_kv` keys: enough chunks for about 1.5 CTAs per SM, each at
-// least WARPS tiles long. n_chunks never decreases with max_kv, so the workspace sized for a
-// cache's capacity covers every position.
+// least CHUNK_KEYS keys long (the kernel uses fewer when the actual length is shorter).
+// n_chunks never decreases with max_kv, so the workspace sized for a cache's capacity covers
+// every position.
 Plan make_plan(int batch, int num_kv_heads, int rows, int max_kv, int head_dim, int sm_count) {
   Plan pl{};
   pl.rows_cta = rows == 1 ? 1 : rows <= 4 ? 4 : 8;
   pl.n_rb = (rows + pl.rows_cta - 1) / pl.rows_cta;
   pl.units = static_cast<int64_t>(batch) * num_kv_heads * pl.n_rb;
-  const int64_t max_chunks = std::max(1, (max_kv + MIN_CHUNK - 1) / MIN_CHUNK);
+  const int64_t max_chunks = std::max(1, (max_kv + CHUNK_KEYS - 1) / CHUNK_KEYS);
   const int64_t want = (3 * static_cast<int64_t>(std::max(sm_count, 1)) / 2 + pl.units - 1) / pl.units;
   pl.n_chunks = static_cast<int>(std::max<int64_t>(1, std::min(max_chunks, want)));
   pl.counters_bytes = round_up(static_cast<size_t>(pl.units) * sizeof(int), 256);
