@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[r][m] = 0ull;
   const T* xb = reinterpret_cast<const T*>(p.x);
-#pragma unroll 2
+#pragma unroll 4  // a 1024-wide row in one round of loads per lane
   for (int c = lane; c < kc; c += 32) {
     uint4 wv[ROWS];
 #pragma unroll
