@@ -175,12 +175,12 @@ def test_kv_append_and_rejects():
                      workspace=torch.zeros(16, dtype=torch.uint8, device="cuda"))
 
 
-def _decoder(num_layers, dtype=torch.float16, seed=0):
-    """The 268M decoder's shapes with fewer layers: (config, fp32 weights as numpy, optimised
-    model without a forward graph)."""
+def _decoder(num_layers, dtype=torch.float16, seed=0, base=None):
+    """A decoder with the 268M shapes (or ``base``'s) and fewer layers: (config, fp32 weights as
+    numpy, optimised model without a forward graph)."""
     import tinker_b200
     from tinker_b200.eager_model import LLAMA_268M, build_model
-    cfg = LLAMA_268M.with_(num_layers=num_layers, max_seq_len=512)
+    cfg = (base or LLAMA_268M).with_(num_layers=num_layers, max_seq_len=512)
     cpu = build_model(cfg, seed=seed)
     weights = {k: v.detach().float().numpy().copy() for k, v in cpu.state_dict().items()}
     model = tinker_b200.optimize(cpu.to("cuda"), dtype=dtype, cuda_graph=False)
@@ -254,3 +254,35 @@ def test_generate_greedy_matches_recompute():
     top2 = full.topk(2, dim=-1).values
     clear = (top2[..., 0] - top2[..., 1]) > 5e-2
     assert torch.equal(full.argmax(-1)[clear], ids[clear])
+
+
+def _shape(name):
+    from tinker_b200.eager_model import LLAMA_268M, QWEN25_05B_SHAPED
+    return {"llama268m": LLAMA_268M, "qwen-shaped": QWEN25_05B_SHAPED,
+            "head_dim128": LLAMA_268M.with_(num_heads=8, num_kv_heads=4, head_dim=128)}[name]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape, dt, tol", [("llama268m", "fp16", 2e-2), ("qwen-shaped", "bf16", 6e-2),
+                                            ("head_dim128", "fp16", 2e-2)])
+def test_chunked_prefill_then_decode(shape, dt, tol):
+    """A prompt in two chunks (the second at position 40 goes through kv_attention: 30 new tokens,
+    up to 210 query rows per kv head), then decode steps; each result equals the matching row of
+    the full forward over all tokens so far. Covers 8-row CTAs (7 query heads per kv head, bf16,
+    tied embeddings) and head_dim 128."""
+    require_b200()
+    import tinker_b200
+    from tinker_b200.eager_model import make_tokens
+    cfg, _, model = _decoder(2, DTYPES[dt], base=_shape(shape))
+    B, steps = 2, 4
+    tokens = make_tokens(cfg, B, 70 + steps, seed=8).cuda()
+    dec = tinker_b200.CachedDecoder(model, batch_size=B, capacity=128)
+    with torch.inference_mode():
+        got = [dec.prefill(tokens[:, :40]).float().clone(), dec.prefill(tokens[:, 40:70]).float().clone()]
+        for t in range(70, 70 + steps):
+            got.append(dec.decode(tokens[:, t]).float().clone())
+        full = model(tokens).float()
+    want = [full[:, 39], full[:, 69]] + [full[:, t] for t in range(70, 70 + steps)]
+    for i, (a, b) in enumerate(zip(got, want)):
+        err = (a - b).abs().max().item()
+        assert err <= tol * max(1.0, b.abs().max().item()), f"result {i}: max |logits - full forward| = {err}"
