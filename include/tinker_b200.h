@@ -179,6 +179,48 @@ TK_API int tk_kv_append(const void* k, int64_t k_tok_stride, const void* v, int6
                         int start_pos, int dtype, void* stream);
 
 /*
+ * One decode step of a whole decoder stack in ONE persistent cooperative kernel (batch <= 8
+ * sequences, one new token each): for every layer the q|k|v product (attention RMSNorm folded
+ * into wq/wk/wv), tk_kv_attention's work, o_proj + residual, gate|up + SwiGLU (FFN RMSNorm folded
+ * into wg/wu), down + residual, separated by grid barriers instead of kernel boundaries; then the
+ * final RMSNorm. The per-block path of the same step is 5 launches per layer (tk_linear /
+ * tk_kv_attention / tk_linear_ex / tk_gate_up_swiglu_ex / tk_linear_ex); the reference has no
+ * cached decoding at all (tinker/modules/attention.py:51, README.md:102).
+ *
+ * tk_decode_step_setup (synchronous, not capturable; zero-fills `scratch` of
+ * tk_decode_step_scratch_bytes() bytes and copies the layer table into it): weights [out, in]
+ * row-major in `dtype`, caches [batch, num_kv_heads, capacity, head_dim], float32 RoPE tables,
+ * `position`: device int32 read when the kernel runs (the first new token's position).
+ * tk_decode_step (capturable): x [batch, hidden] holds the embedding rows and is overwritten
+ * with the last block's output; y [batch, hidden] receives the final RMSNorm of it. Appends the
+ * step's keys and values to the caches. Waits are bounded; a device error stops the step.
+ */
+typedef struct tk_step_layer {
+  const void* wq;
+  const void* wk;
+  const void* wv;
+  const void* wo;
+  const void* wg;
+  const void* wu;
+  const void* wd;
+  void* k_cache;
+  void* v_cache;
+  float eps_attn;
+  float eps_ffn;
+} tk_step_layer;
+
+TK_API int64_t tk_decode_step_scratch_bytes(int num_layers, int batch, int hidden, int num_heads, int num_kv_heads,
+                                            int head_dim, int intermediate, int capacity);
+TK_API int tk_decode_step_setup(const tk_step_layer* layers, int num_layers, int batch, int hidden, int num_heads,
+                                int num_kv_heads, int head_dim, int intermediate, const float* cos_table,
+                                const float* sin_table, int64_t table_rows, int capacity, const int* position,
+                                const void* final_norm_weight, float final_eps, int dtype, void* scratch,
+                                int64_t scratch_bytes);
+TK_API int tk_decode_step(void* x, void* y, void* scratch, void* stream);
+/* Forget the plan tk_decode_step_setup stored for `scratch` (before freeing it). */
+TK_API int tk_decode_step_release(void* scratch);
+
+/*
  * Epilogue options of tk_linear_ex / tk_gate_up_swiglu_ex (zero-initialise, then set):
  *  residual       [m, n] with y's row stride, added before the one rounding (plain store).
  *  row_ssq_in     [row_ssq_parts, m] float32 partial sums of squares of x's rows: the

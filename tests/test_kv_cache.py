@@ -188,18 +188,20 @@ def _decoder(num_layers, dtype=torch.float16, seed=0, base=None):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("fused_step", [True, False])
 @pytest.mark.parametrize("prompt_len", [100, 8])
-def test_cached_decoder_matches_full_forward(prompt_len):
+def test_cached_decoder_matches_full_forward(prompt_len, fused_step):
     """Prefill (tensor-core prompt path at 100 tokens, the kv_attention path at 8) then 16 decode
-    steps through the CUDA graph: every step's logits equal the last row of the full forward of
-    the same model over all tokens so far."""
+    steps through the CUDA graph, with the one-kernel step or the per-block kernels: every step's
+    logits equal the last row of the full forward of the same model over all tokens so far."""
     require_b200()
     import tinker_b200
     from tinker_b200.eager_model import make_tokens
     cfg, _, model = _decoder(4)
     B, steps = 2, 16
     tokens = make_tokens(cfg, B, prompt_len + steps, seed=3).cuda()
-    dec = tinker_b200.CachedDecoder(model, batch_size=B, capacity=256, cuda_graph=True)
+    dec = tinker_b200.CachedDecoder(model, batch_size=B, capacity=256, cuda_graph=True, fused_step=fused_step)
+    assert dec.fused_step == fused_step
     with torch.inference_mode():
         got = [dec.prefill(tokens[:, :prompt_len]).float().clone()]
         for t in range(prompt_len, prompt_len + steps):
@@ -286,3 +288,56 @@ def test_chunked_prefill_then_decode(shape, dt, tol):
     for i, (a, b) in enumerate(zip(got, want)):
         err = (a - b).abs().max().item()
         assert err <= tol * max(1.0, b.abs().max().item()), f"result {i}: max |logits - full forward| = {err}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape, dt, B", [("llama268m", "fp16", 1), ("llama268m", "bf16", 3), ("qwen-shaped", "bf16", 8),
+                                          ("head_dim128", "fp16", 5)])
+def test_fused_step_matches_per_block_step(shape, dt, B):
+    """The one-kernel decode step (grid barriers between the phases) against the per-block kernels
+    on the same model, cache contents and tokens: logits and the cache rows it appends agree to
+    the rounding of the fp32 sums (different summation order and row-statistics parts)."""
+    require_b200()
+    import tinker_b200
+    from tinker_b200.eager_model import make_tokens
+    cfg, _, model = _decoder(3, DTYPES[dt], base=_shape(shape))
+    P, steps = 30, 5
+    tokens = make_tokens(cfg, B, P + steps, seed=11).cuda()
+    outs, caches = [], []
+    for fused in (True, False):
+        dec = tinker_b200.CachedDecoder(model, batch_size=B, capacity=64, fused_step=fused)
+        with torch.inference_mode():
+            dec.prefill(tokens[:, :P])
+            steps_out = [dec.decode(tokens[:, t]).float().clone() for t in range(P, P + steps)]
+        outs.append(torch.stack(steps_out))
+        caches.append((dec.cache.k[:, :, :, :P + steps].float().clone(), dec.cache.v[:, :, :, :P + steps].float().clone()))
+        dec.release()
+    scale = outs[1].abs().max().item()
+    assert (outs[0] - outs[1]).abs().max().item() <= 2e-2 * max(1.0, scale)
+    for a, b in zip(caches[0], caches[1]):
+        assert (a - b).abs().max().item() <= 5e-2 * max(1.0, b.abs().max().item())
+
+
+@pytest.mark.gpu
+def test_fused_step_stops_on_device_error():
+    """A position past the cache: the attention phase records device error 2 and every CTA leaves
+    at the next grid barrier (no wait runs out); the decoder is usable again after clearing it."""
+    require_b200()
+    import tinker_b200
+    from tinker_b200 import _lib
+    from tinker_b200.eager_model import make_tokens
+    cfg, _, model = _decoder(2)
+    tokens = make_tokens(cfg, 1, 12, seed=12).cuda()
+    dec = tinker_b200.CachedDecoder(model, batch_size=1, capacity=16, cuda_graph=False, fused_step=True)
+    _lib.device_error(clear=True)
+    with torch.inference_mode():
+        dec.prefill(tokens[:, :10])
+        dec._setup_step()
+        dec.cache.position.fill_(16)  # start + 1 > capacity
+        dec._fused_forward(tokens[:, 10:11])
+        torch.cuda.synchronize()
+        assert _lib.device_error(clear=True) == 2
+        lg = dec.decode(tokens[:, 10])  # position 10 again, now in range
+        torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
+    assert torch.isfinite(lg.float()).all()

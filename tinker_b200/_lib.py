@@ -36,6 +36,12 @@ class Epilogue(ctypes.Structure):
 
 _EPI = ctypes.POINTER(Epilogue)
 
+
+class StepLayer(ctypes.Structure):
+    """``tk_step_layer`` of tinker_b200.h: one layer of tk_decode_step_setup's table."""
+    _fields_ = [("wq", _P), ("wk", _P), ("wv", _P), ("wo", _P), ("wg", _P), ("wu", _P), ("wd", _P),
+                ("k_cache", _P), ("v_cache", _P), ("eps_attn", _F), ("eps_ffn", _F)]
+
 # name -> argtypes; every entry point returns int (status)
 SIGNATURES = {
     "tk_version": [],
@@ -60,10 +66,15 @@ SIGNATURES = {
                         _P, _P, _I64, _I, _P],
     "tk_kv_attention_workspace": [_I, _I, _I, _I, _I, _I],
     "tk_kv_append": [_P, _I64, _P, _I64, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
+    "tk_decode_step_scratch_bytes": [_I, _I, _I, _I, _I, _I, _I, _I],
+    "tk_decode_step_setup": [ctypes.POINTER(StepLayer), _I, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I, _P, _P, _F, _I,
+                             _P, _I64],
+    "tk_decode_step": [_P, _P, _P, _P],
+    "tk_decode_step_release": [_P],
 }
 
 # entry points whose return value is not a status
-RESTYPES = {"tk_kv_attention_workspace": _I64}
+RESTYPES = {"tk_kv_attention_workspace": _I64, "tk_decode_step_scratch_bytes": _I64}
 
 _lock = threading.Lock()
 _lib = None
