@@ -38,6 +38,29 @@ namespace kvattn {
 template <int DT, int D, int R>
 __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  {
+    // The cached rows below the position were written by earlier steps, not by the previous kernel:
+    // pull this CTA's share into L2 while that kernel finishes (a hint only, so a position that
+    // is about to change does no harm).
+    const int start = p.start_dev ? *p.start_dev : p.start_pos;
+    const int kv_len = start + p.seq;
+    if (start > 0 && kv_len <= p.cap) {
+      const int n_chunks = min(p.n_chunks, (kv_len + CHUNK_KEYS - 1) / CHUNK_KEYS);
+      const int n_tiles = (kv_len + KT - 1) / KT;
+      const int per = (n_tiles + n_chunks - 1) / n_chunks;
+      const int lo = blockIdx.x * per * KT, hi = min(start, lo + per * KT);
+      if (static_cast<int>(blockIdx.x) < n_chunks && lo < hi) {
+        const int64_t row0 = (static_cast<int64_t>(blockIdx.z) * p.num_kv_heads + blockIdx.y / p.n_rb) * p.cap + lo;
+        const int64_t bytes = static_cast<int64_t>(hi - lo) * D * 2;
+        const char* kc = static_cast<const char*>(p.kc) + row0 * D * 2;
+        const char* vc = static_cast<const char*>(p.vc) + row0 * D * 2;
+        for (int64_t o = static_cast<int64_t>(threadIdx.x) * 128; o < bytes; o += THREADS * 128) {
+          prefetch_l2(kc + o);
+          prefetch_l2(vc + o);
+        }
+      }
+    }
+  }
   pdl_wait();  // q/k/v come from the previous kernel; the position may be written just before
   kv_attention_item<DT, D, R>(p, blockIdx.x, blockIdx.y / p.n_rb, blockIdx.y % p.n_rb, blockIdx.z,
                               blockIdx.z * gridDim.y + blockIdx.y,
