@@ -40,15 +40,16 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   {
     // The cached rows below the position were written by earlier steps, not by the previous kernel:
-    // pull this CTA's share into L2 while that kernel finishes (a hint only, so a position that
-    // is about to change does no harm).
+    // pull the first CHUNK_KEYS of this CTA's share into L2 while that kernel finishes (a hint
+    // only, so a position that is about to change does no harm; longer ranges are left to the
+    // cp.async pipeline, which a larger prefetch only competes with).
     const int start = p.start_dev ? *p.start_dev : p.start_pos;
     const int kv_len = start + p.seq;
     if (start > 0 && kv_len <= p.cap) {
       const int n_chunks = min(p.n_chunks, (kv_len + CHUNK_KEYS - 1) / CHUNK_KEYS);
       const int n_tiles = (kv_len + KT - 1) / KT;
       const int per = (n_tiles + n_chunks - 1) / n_chunks;
-      const int lo = blockIdx.x * per * KT, hi = min(start, lo + per * KT);
+      const int lo = blockIdx.x * per * KT, hi = min(min(start, lo + per * KT), lo + CHUNK_KEYS);
       if (static_cast<int>(blockIdx.x) < n_chunks && lo < hi) {
         const int64_t row0 = (static_cast<int64_t>(blockIdx.z) * p.num_kv_heads + blockIdx.y / p.n_rb) * p.cap + lo;
         const int64_t bytes = static_cast<int64_t>(hi - lo) * D * 2;
