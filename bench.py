@@ -62,7 +62,7 @@ def _args():
     ap.add_argument("--qwen-batch", type=int, default=64)
     ap.add_argument("--sweep", default=None, metavar="KINDS",
                     help="run the standalone sweeps instead (comma list of rmsnorm, ffn, attention, model1b; "
-                         "tinker_b200.sweep), one JSON line per case")
+                         "bench_sweep.py), one JSON line per case")
     return ap.parse_args()
 
 
@@ -102,7 +102,7 @@ def _oracle_setup(cfg, seed=0):
     import numpy as np
     import oracle
     _use_all_host_threads()
-    from tinker_b200.eager_model import build_model
+    from bench_model import build_model
     m = build_model(cfg, seed=seed)
     w = {k: v.detach().float().numpy() for k, v in m.state_dict().items()}
     ocfg = oracle.ModelConfig(**{f: getattr(cfg, f) for f in oracle.ModelConfig.__dataclass_fields__})
@@ -131,7 +131,7 @@ def run_reference(args):
         return  # the CPU reference runs once, on rank 0
     import numpy as np
     import oracle
-    from tinker_b200.eager_model import LLAMA_268M, make_tokens
+    from bench_model import LLAMA_268M, make_tokens
     cfg = LLAMA_268M
     tokens = make_tokens(cfg, 1, 128, seed=1)
     oracle_mod, w, ocfg, _ = _oracle_setup(cfg)
@@ -388,7 +388,7 @@ def _decode_bench(dev, peaks, peak_note, batch: int, prompt: int = DECODE_PROMPT
     import torch
     import tinker_b200
     from tinker_b200 import _lib
-    from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
+    from bench_model import LLAMA_268M, build_model, make_tokens
     cfg = LLAMA_268M
     model = tinker_b200.optimize(build_model(cfg, seed=0).to(dev), dtype=torch.float16, cuda_graph=False)
     dec = tinker_b200.CachedDecoder(model, batch_size=batch, capacity=prompt + new + 1)
@@ -502,7 +502,7 @@ def run_only(args):
     shapes (``--only forward`` / ``--only gate_up_swiglu`` ...) and print its mean time."""
     import torch
     import tinker_b200
-    from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
+    from bench_model import LLAMA_268M, build_model, make_tokens
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     if args.only in ("decode", "kv_attention"):
@@ -515,7 +515,7 @@ def run_only(args):
                   flush=True)
         return
     if args.only == "qwen_forward":
-        from tinker_b200.eager_model import QWEN25_05B_SHAPED
+        from bench_model import QWEN25_05B_SHAPED
         qcfg = QWEN25_05B_SHAPED
         qtok = make_tokens(qcfg, args.qwen_batch, 512, seed=7)
         qm = tinker_b200.optimize(build_model(qcfg, seed=0).to(dev), dtype=torch.bfloat16, cuda_graph=True,
@@ -561,7 +561,7 @@ def run_ours(args):
     import torch
     import tinker_b200
     from tinker_b200 import _lib
-    from tinker_b200.eager_model import LLAMA_268M, QWEN25_05B_SHAPED, build_model, make_tokens
+    from bench_model import LLAMA_268M, QWEN25_05B_SHAPED, build_model, make_tokens
 
     rank, world, dev = _dist_init(args)
     peaks, peak_note = _peaks()
@@ -705,7 +705,7 @@ def run_ours(args):
 def main():
     args = _args()
     if args.sweep:
-        from tinker_b200 import sweep
+        import bench_sweep as sweep
         sweep.main(["--only", args.sweep])
     elif args.impl == "reference":
         run_reference(args)

@@ -196,7 +196,7 @@ def _time_replays(graph, reps: int) -> float:
 
 def sweep_model1b(peaks, emit):
     import tinker_b200
-    from tinker_b200.eager_model import LLAMA_1B, build_model, make_tokens
+    from bench_model import LLAMA_1B, build_model, make_tokens
     cfg = LLAMA_1B
     ref_model = build_model(cfg, seed=0).to("cuda", torch.float16).eval()
     params = sum(p.numel() for p in ref_model.parameters())

@@ -1,67 +1,29 @@
-"""Plain-PyTorch Llama-style decoder: the user model that ``optimize()`` patches.
+"""The reference's own eager PyTorch decoder (test infrastructure only).
 
-The blocks have the structure, attribute names and arithmetic of the model the
-reference benchmarks (eb1386/TinKer benchmarks/bench_e2e.py:17-138), wrapped
-with a token embedding and an LM head as in examples/patch_any_model.py:95-108.
-Nothing here calls the CUDA extension: this is the *unpatched* eager model, the
-reference's own eager path, and what ``patch_model`` rewrites in place.
+TEST INFRASTRUCTURE, like the rest of ``oracle/``: the blocks below are the model the
+reference benchmarks (eb1386/TinKer benchmarks/bench_e2e.py:17-138: ``RMSNorm``,
+``SwiGLUFFN``, ``GQAAttention``, ``TransformerBlock`` and the layer stack of
+``SimpleTransformer``), kept with the reference's own arithmetic and wrapped with the
+token embedding and LM head of examples/patch_any_model.py:95-108. They are carried
+here because the reference checkout cannot travel to the GPU host. Uses:
 
-``init_weights`` fills parameters deterministically (sorted ``state_dict``
-names, one ``torch.Generator``), so the same seed gives identical weights in the
-reference's own classes and in these.
+* the CPU baseline: ``bench.py`` times this model's fp32 eager forward on the host
+  cores (the reference's unpatched CPU path);
+* the reference's half-precision eager error on the GPU, which the parity tests use as
+  the bar the CUDA path must not be worse than;
+* ``tests/golden/make_golden.py`` initialises the reference's own classes with
+  ``init_weights`` and records their logits, which pins this copy (and the numpy
+  oracle) to the reference.
+
+Any config object with the fields of ``bench_model.DecoderConfig`` works. Nothing in
+the product package imports this file.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass, replace
-
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
-
-
-@dataclass(frozen=True)
-class DecoderConfig:
-    vocab_size: int
-    hidden_size: int
-    num_layers: int
-    num_heads: int
-    num_kv_heads: int
-    head_dim: int
-    intermediate_size: int
-    eps: float = 1e-6
-    rope_theta: float = 10000.0
-    tied_embeddings: bool = False
-    max_seq_len: int = 2048
-
-    def with_(self, **kw) -> "DecoderConfig":
-        return replace(self, **kw)
-
-    def num_params(self) -> int:
-        h, d = self.hidden_size, self.head_dim
-        attn = h * (self.num_heads * d) * 2 + h * (self.num_kv_heads * d) * 2
-        ffn = 3 * h * self.intermediate_size
-        layer = attn + ffn + 2 * h
-        emb = self.vocab_size * h * (1 if self.tied_embeddings else 2)
-        return self.num_layers * layer + h + emb
-
-
-# The decoder shapes the workloads are quoted on.
-LLAMA_268M = DecoderConfig(vocab_size=32000, hidden_size=1024, num_layers=18, num_heads=16,
-                           num_kv_heads=4, head_dim=64, intermediate_size=2816, eps=1e-6,
-                           rope_theta=10000.0, tied_embeddings=False)
-QWEN25_05B_SHAPED = DecoderConfig(vocab_size=151936, hidden_size=896, num_layers=24, num_heads=14,
-                                  num_kv_heads=2, head_dim=64, intermediate_size=4864, eps=1e-6,
-                                  rope_theta=1e6, tied_embeddings=True)
-LLAMA_1B = DecoderConfig(vocab_size=32000, hidden_size=2048, num_layers=16, num_heads=32,
-                         num_kv_heads=8, head_dim=64, intermediate_size=5632, eps=1e-5,
-                         rope_theta=10000.0, tied_embeddings=False)
-TINY = DecoderConfig(vocab_size=256, hidden_size=128, num_layers=2, num_heads=2, num_kv_heads=1,
-                     head_dim=64, intermediate_size=256, eps=1e-6, rope_theta=10000.0,
-                     tied_embeddings=False, max_seq_len=256)
-
-PRESETS = {"llama268m": LLAMA_268M, "qwen25-0.5b-shaped": QWEN25_05B_SHAPED,
-           "llama1b": LLAMA_1B, "tiny": TINY}
 
 
 class RMSNorm(nn.Module):
@@ -139,7 +101,7 @@ class GQAAttention(nn.Module):
 class TransformerBlock(nn.Module):
     """bench_e2e.py:97-115 (pre-norm, residual adds in the model dtype)."""
 
-    def __init__(self, cfg: DecoderConfig):
+    def __init__(self, cfg):
         super().__init__()
         self.attn_norm = RMSNorm(cfg.hidden_size, cfg.eps)
         self.attn = GQAAttention(cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
@@ -153,10 +115,10 @@ class TransformerBlock(nn.Module):
         return x
 
 
-class DecoderLM(nn.Module):
+class ReferenceLM(nn.Module):
     """Embedding -> blocks -> final RMSNorm -> LM head (examples/patch_any_model.py:95-108)."""
 
-    def __init__(self, cfg: DecoderConfig):
+    def __init__(self, cfg):
         super().__init__()
         self.config = cfg
         self.embedding = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
@@ -203,14 +165,9 @@ def init_weights(model: nn.Module, seed: int = 0, std: float = 0.02,
     return model
 
 
-def build_model(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=torch.float32) -> DecoderLM:
-    """Seeded random-weight model, weights drawn on the CPU then moved."""
-    model = DecoderLM(cfg)
+def build_model(cfg, seed: int = 0, device="cpu", dtype=torch.float32) -> ReferenceLM:
+    """Seeded random-weight reference model, weights drawn on the CPU then moved."""
+    model = ReferenceLM(cfg)
     init_weights(model, seed)
     return model.to(device=device, dtype=dtype).eval()
 
-
-def make_tokens(cfg: DecoderConfig, batch: int, seq: int, seed: int = 1) -> torch.Tensor:
-    """Token ids uniform in [0, vocab) from their own CPU generator."""
-    gen = torch.Generator().manual_seed(seed)
-    return torch.randint(0, cfg.vocab_size, (batch, seq), generator=gen)

@@ -25,7 +25,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
-from tinker_b200.eager_model import LLAMA_268M, TINY, init_weights, make_tokens  # noqa: E402
+from bench_model import LLAMA_268M, TINY, init_weights, make_tokens  # noqa: E402
 
 
 def _f32(t: torch.Tensor) -> np.ndarray:
@@ -71,8 +71,11 @@ def _ref_lm(be, cfg):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("TINKER_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("TINKER_REFERENCE"),
+                    help="path of the eb1386/TinKer checkout (or set TINKER_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference PATH or the TINKER_REFERENCE variable")
     tinker, fa, fr, fs, be = _load_reference(args.reference)
     dt = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
 

@@ -179,7 +179,7 @@ def _decoder(num_layers, dtype=torch.float16, seed=0, base=None):
     """A decoder with the 268M shapes (or ``base``'s) and fewer layers: (config, fp32 weights as
     numpy, optimised model without a forward graph)."""
     import tinker_b200
-    from tinker_b200.eager_model import LLAMA_268M, build_model
+    from bench_model import LLAMA_268M, build_model
     cfg = (base or LLAMA_268M).with_(num_layers=num_layers, max_seq_len=512)
     cpu = build_model(cfg, seed=seed)
     weights = {k: v.detach().float().numpy().copy() for k, v in cpu.state_dict().items()}
@@ -196,7 +196,7 @@ def test_cached_decoder_matches_full_forward(prompt_len, fused_step):
     logits equal the last row of the full forward of the same model over all tokens so far."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, _, model = _decoder(4)
     B, steps = 2, 16
     tokens = make_tokens(cfg, B, prompt_len + steps, seed=3).cuda()
@@ -220,7 +220,7 @@ def test_cached_decoder_matches_oracle_and_eager_steps():
     algorithm over the whole sequence), and the graph steps vs eager (no graph) steps."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, w, model = _decoder(3)
     B, P, steps = 1, 40, 6
     tokens = make_tokens(cfg, B, P + steps, seed=4)
@@ -244,7 +244,7 @@ def test_generate_greedy_matches_recompute():
     the full forward over the sequence so far picks (random weights give near-ties)."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, _, model = _decoder(2)
     B, P, n = 2, 24, 12
     prompt = make_tokens(cfg, B, P, seed=6).cuda()
@@ -259,7 +259,7 @@ def test_generate_greedy_matches_recompute():
 
 
 def _shape(name):
-    from tinker_b200.eager_model import LLAMA_268M, QWEN25_05B_SHAPED
+    from bench_model import LLAMA_268M, QWEN25_05B_SHAPED
     return {"llama268m": LLAMA_268M, "qwen-shaped": QWEN25_05B_SHAPED,
             "head_dim128": LLAMA_268M.with_(num_heads=8, num_kv_heads=4, head_dim=128)}[name]
 
@@ -274,7 +274,7 @@ def test_chunked_prefill_then_decode(shape, dt, tol):
     tied embeddings) and head_dim 128."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, _, model = _decoder(2, DTYPES[dt], base=_shape(shape))
     B, steps = 2, 4
     tokens = make_tokens(cfg, B, 70 + steps, seed=8).cuda()
@@ -299,7 +299,7 @@ def test_fused_step_matches_per_block_step(shape, dt, B):
     the rounding of the fp32 sums (different summation order and row-statistics parts)."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, _, model = _decoder(3, DTYPES[dt], base=_shape(shape))
     P, steps = 30, 5
     tokens = make_tokens(cfg, B, P + steps, seed=11).cuda()
@@ -325,7 +325,7 @@ def test_fused_step_stops_on_device_error():
     require_b200()
     import tinker_b200
     from tinker_b200 import _lib
-    from tinker_b200.eager_model import make_tokens
+    from bench_model import make_tokens
     cfg, _, model = _decoder(2)
     tokens = make_tokens(cfg, 1, 12, seed=12).cuda()
     dec = tinker_b200.CachedDecoder(model, batch_size=1, capacity=16, cuda_graph=False, fused_step=True)

@@ -40,13 +40,14 @@ def _stats(logits, ref):
 def test_llama268m_b1s128_fp16_graph():
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import LLAMA_268M, build_model, make_tokens
+    from bench_model import LLAMA_268M, build_model, make_tokens
     cfg = LLAMA_268M
     tokens = make_tokens(cfg, 1, 128, seed=1)
     cpu_model = build_model(cfg, seed=0)
     ref = _oracle_logits(cpu_model, tokens, cfg).astype(np.float64)
 
-    eager16 = build_model(cfg, seed=0, device="cuda", dtype=torch.float16)
+    from oracle.torch_model import build_model as build_reference
+    eager16 = build_reference(cfg, seed=0, device="cuda", dtype=torch.float16)  # the reference's fp16 eager path
     with torch.inference_mode():
         base = np32(eager16(tokens.cuda()))
     base_err, base_top1, _ = _stats(base, ref)
@@ -71,7 +72,7 @@ def test_llama268m_b1s128_fp16_graph():
 def test_tiny_model_patched_eager(dtype):
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    from bench_model import TINY, build_model, make_tokens
     tokens = make_tokens(TINY, 3, 40, seed=2)
     cpu_model = build_model(TINY, seed=3)
     ref = _oracle_logits(cpu_model, tokens, TINY).astype(np.float64)
@@ -88,7 +89,7 @@ def test_qwen_shaped_two_layers_bf16():
     """Qwen2.5-0.5B shapes (hidden 896, 14/2 heads, FFN 4864, theta 1e6, tied head), 2 layers, bf16."""
     require_b200()
     import tinker_b200
-    from tinker_b200.eager_model import QWEN25_05B_SHAPED, build_model, make_tokens
+    from bench_model import QWEN25_05B_SHAPED, build_model, make_tokens
     cfg = QWEN25_05B_SHAPED.with_(num_layers=2, vocab_size=4096)
     tokens = make_tokens(cfg, 2, 512, seed=4)
     cpu_model = build_model(cfg, seed=5)
@@ -106,7 +107,7 @@ def test_block_fusion_matches_unfused_and_skips_other_structures():
     require_b200()
     import torch.nn as nn
     import tinker_b200
-    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    from bench_model import TINY, build_model, make_tokens
     from tinker_b200.fusion import fuse_decoder_blocks
     cfg = TINY.with_(num_layers=3)
     tokens = make_tokens(cfg, 2, 64, seed=9).cuda()
@@ -137,7 +138,7 @@ def test_folded_norms_match_unfolded_and_follow_weight_updates():
     require_b200()
     import tinker_b200
     from tinker_b200 import _lib
-    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    from bench_model import TINY, build_model, make_tokens
     cfg = TINY.with_(num_layers=3)
     tokens = make_tokens(cfg, 2, 96, seed=5).cuda()
     a = tinker_b200.optimize(build_model(cfg, seed=8).cuda(), dtype=torch.float16, fold_norms=False)
@@ -166,7 +167,7 @@ def test_folded_norm_statistics_follow_in_place_changes():
     require_b200()
     import torch.nn as nn
     import tinker_b200
-    from tinker_b200.eager_model import TINY, build_model, make_tokens
+    from bench_model import TINY, build_model, make_tokens
 
     class Scaled(nn.Module):  # x = block(x); x *= 1.5 (in place) between blocks
         def __init__(self, lm):

@@ -94,21 +94,27 @@ def _weights_np(model):
 
 
 def test_tiny_model_matches_reference():
-    from tinker_b200.eager_model import TINY, build_model
+    from bench_model import TINY, build_model
     z = _load("tiny_model.npz")
     m = build_model(TINY, seed=int(z["weight_seed"]))
     cfg = oracle.ModelConfig(**{f: getattr(TINY, f) for f in oracle.ModelConfig.__dataclass_fields__})
     logits = oracle.forward_logits(_weights_np(m), z["tokens"], cfg)
     np.testing.assert_allclose(logits, z["logits"], atol=2e-5, rtol=1e-4)
-    # the eager torch model in this repo is the same model as the reference's
+    # both eager torch models give the reference's logits: the copy of the reference's own
+    # blocks (oracle/torch_model.py, the CPU baseline) and the bench's user model
+    # (bench_model.py, written independently), from the same seeded weights
+    from oracle.torch_model import build_model as build_reference
+    ref_model = build_reference(TINY, seed=int(z["weight_seed"]))
+    assert ref_model.state_dict().keys() == m.state_dict().keys()
+    tok = torch.from_numpy(z["tokens"])
     with torch.inference_mode():
-        t = m(torch.from_numpy(z["tokens"])).numpy()
-    np.testing.assert_allclose(t, z["logits"], atol=1e-5, rtol=1e-5)
+        for model in (ref_model, m):
+            np.testing.assert_allclose(model(tok).numpy(), z["logits"], atol=1e-5, rtol=1e-5)
 
 
 @pytest.mark.slow
 def test_llama268m_logits_match_reference():
-    from tinker_b200.eager_model import LLAMA_268M, build_model
+    from bench_model import LLAMA_268M, build_model
     z = _load("llama268m_b1s128.npz")
     m = build_model(LLAMA_268M, seed=int(z["weight_seed"]))
     cfg = oracle.ModelConfig(**{f: getattr(LLAMA_268M, f) for f in oracle.ModelConfig.__dataclass_fields__})

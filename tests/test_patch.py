@@ -7,7 +7,7 @@ import torch
 import torch.nn as nn
 
 import tinker_b200
-from tinker_b200.eager_model import TINY, LLAMA_268M, DecoderLM, build_model
+from bench_model import TINY, LLAMA_268M, DecoderLM, build_model
 from tinker_b200.modules import TinKerAttention, TinKerRMSNorm, TinKerSwiGLU
 from tinker_b200.patch import _is_gqa_attention, _is_rmsnorm, _is_swiglu
 
@@ -170,3 +170,75 @@ def test_rope_tables_are_shared_across_layers():
     assert m.layers[0].attn.cos_table is m.layers[2].attn.cos_table
     m.to(torch.float16)
     assert m.layers[1].attn.sin_table.dtype == torch.float32
+
+
+# ---- decisions pinned to the reference's patch_model ------------------------------------------
+def _zoo():
+    import importlib
+    import os
+    import sys
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    if here not in sys.path:
+        sys.path.insert(0, here)
+    return importlib.import_module("patch_zoo")
+
+
+@pytest.mark.parametrize("flags", ["all", "no_norm", "no_ffn", "no_attention", "theta_arg"])
+def test_patch_decisions_match_the_reference(flags):
+    """The reference's own patch_model, run over the module zoo of tests/golden/patch_zoo.py by
+    make_patch_golden.py, replaced exactly these children with exactly these sizes."""
+    import json
+    import os
+    zoo = _zoo()
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "patch_decisions.json")) as f:
+        want = json.load(f)[flags]
+    got = zoo.describe(tinker_b200.patch_model(zoo.zoo(), **zoo.FLAG_SETS[flags]))
+    assert got == want
+
+
+def test_reference_dummy_modules_from_module():
+    """The source modules of the reference's from_module tests (tests/test_attention.py:171-180,
+    tests/test_rmsnorm.py:71-77, tests/test_swiglu.py:77-87): sizes, epsilon and weights carry over."""
+    torch.manual_seed(0)
+    src = nn.Module()
+    src.head_dim = 64
+    src.q_proj, src.k_proj = nn.Linear(512, 512, bias=False), nn.Linear(512, 128, bias=False)
+    src.v_proj, src.o_proj = nn.Linear(512, 128, bias=False), nn.Linear(512, 512, bias=False)
+    att = TinKerAttention.from_module(src.to(torch.bfloat16))
+    assert (att.num_heads, att.num_kv_heads, att.head_dim) == (8, 2, 64)
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        assert torch.equal(getattr(att, n).weight.to(torch.bfloat16), getattr(src, n).weight)
+
+    norm = nn.Module()
+    norm.eps = 1e-5
+    norm.weight = nn.Parameter(torch.randn(512))
+    tn = TinKerRMSNorm.from_module(norm)
+    assert tn.eps == 1e-5 and torch.equal(tn.weight, norm.weight)
+
+    ffn = nn.Module()
+    ffn.gate_proj, ffn.up_proj = nn.Linear(512, 1376, bias=False), nn.Linear(512, 1376, bias=False)
+    ffn.down_proj = nn.Linear(1376, 512, bias=False)
+    tf = TinKerSwiGLU.from_module(ffn)
+    assert (tf.hidden_size, tf.intermediate_size) == (512, 1376)
+    for n in ("gate_proj", "up_proj", "down_proj"):
+        assert torch.equal(getattr(tf, n).weight, getattr(ffn, n).weight)
+
+
+def test_benchmark_model_reports_the_reference_keys():
+    """benchmark_model on a CPU model: the reference's result keys, a consistent median/min/mean
+    and tokens/s at the median."""
+    from tinker_b200 import benchmark_model
+
+    class Toy(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.emb = nn.Embedding(50, 8)
+
+        def forward(self, t):
+            return self.emb(t).sum(-1)
+
+    r = benchmark_model(Toy(), input_shape=(2, 16), vocab_size=50, warmup=2, runs=9, device="cpu")
+    assert set(r) == {"median_ms", "mean_ms", "min_ms", "tokens_per_sec", "device"}
+    assert r["device"] == "cpu"
+    assert 0 <= r["min_ms"] <= r["median_ms"]
+    assert r["tokens_per_sec"] == pytest.approx(32 / (r["median_ms"] / 1e3), rel=0.05, abs=1)

@@ -38,7 +38,7 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from tinker_b200.eager_model import TINY, build_model, make_tokens
+        from bench_model import TINY, build_model, make_tokens
         from tinker_b200.replicas import gather_batch, local_shard
         torch.set_num_threads(1)
         model = build_model(TINY, seed=3)

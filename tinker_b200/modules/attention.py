@@ -1,4 +1,4 @@
-"""fused attention module (drop-in for eb1386/TinKer tinker/modules/attention.py:9-153).
+"""Fused attention module (drop-in for eb1386/TinKer tinker/modules/attention.py:9-124).
 
 ``forward`` runs three kernels: the q|k|v projection as one tcgen05 GEMM over
 the three weights (no concatenated copy) whose epilogue applies RoPE to the q
@@ -17,6 +17,7 @@ import torch.nn as nn
 from tinker_b200.kernels.fused_attention import causal_attention, fused_attention, precompute_rope_tables
 from tinker_b200.kernels.gemm import linear, linear_rope
 from tinker_b200.kernels.kv_cache import kv_append, kv_attention
+from tinker_b200.modules._roles import attention_projections
 
 # Query rows per kv head (groups * new tokens) above which a prompt at position 0 runs on the
 # tensor-core attention kernel before its keys/values are appended to the cache; below it the
@@ -25,16 +26,16 @@ PROMPT_MIN_ROWS = 64
 
 
 class TinKerAttention(nn.Module):
-    """fused rope+gqa attention
+    """Causal grouped-query attention with interleaved-pair RoPE on this library's kernels.
 
     args:
-        hidden_size: hidden dim
+        hidden_size: model width (input and output features)
         num_heads: query heads
-        num_kv_heads: kv heads
-        head_dim: per-head dim
-        rope_theta: rope base
-        max_seq_len: max length
-        dropout: attn dropout (inference only; accepted for signature compatibility)
+        num_kv_heads: key/value heads (a divisor of num_heads; 1 = MQA, num_heads = MHA)
+        head_dim: features per head (default hidden_size // num_heads)
+        rope_theta: RoPE frequency base
+        max_seq_len: rows of the RoPE tables (the largest position + 1)
+        dropout: accepted for signature compatibility; inference only, never applied
     """
 
     def __init__(
@@ -137,86 +138,37 @@ class TinKerAttention(nn.Module):
                             self.head_dim, start_pos, position, kv_cache.workspace(S))
 
     @classmethod
-    def from_module(
-        cls,
-        source: nn.Module,
-        rope_theta: float = 10000.0,
-        max_seq_len: int = 2048,
-    ) -> "TinKerAttention":
-        """from existing module (head-dim / head-count inference as attention.py:74-117)"""
-        q_proj, k_proj, v_proj, o_proj = _find_attention_projections(source)
+    def from_module(cls, source: nn.Module, rope_theta: float = 10000.0, max_seq_len: int = 2048) -> "TinKerAttention":
+        """A ``TinKerAttention`` holding copies of ``source``'s q/k/v/o projection weights.
 
-        hidden_size = q_proj.weight.shape[1]
-        q_out = q_proj.weight.shape[0]
-        kv_out = k_proj.weight.shape[0]
-
-        head_dim = getattr(source, "head_dim", None)
-        if head_dim is None:
-            for candidate in [64, 128]:
-                if q_out % candidate == 0 and kv_out % candidate == 0:
-                    head_dim = candidate
-                    break
-            if head_dim is None:
-                head_dim = hidden_size // (q_out // (kv_out // 1))
-
-        num_heads = q_out // head_dim
-        num_kv_heads = kv_out // head_dim
-
-        source_theta = getattr(source, "rope_theta", None)
-        if source_theta is not None:
-            rope_theta = source_theta
-
-        module = cls(
-            hidden_size=hidden_size,
-            num_heads=num_heads,
-            num_kv_heads=num_kv_heads,
-            head_dim=head_dim,
-            rope_theta=rope_theta,
-            max_seq_len=max_seq_len,
-        )
-
-        module.q_proj.weight.data.copy_(q_proj.weight.data)
-        module.k_proj.weight.data.copy_(k_proj.weight.data)
-        module.v_proj.weight.data.copy_(v_proj.weight.data)
-        module.o_proj.weight.data.copy_(o_proj.weight.data)
-
-        device = q_proj.weight.device
-        module.cos_table = module.cos_table.to(device)
-        module.sin_table = module.sin_table.to(device)
+        The head layout comes from the weight shapes: ``source.head_dim`` when it has
+        one, else the first of 64 and 128 that divides both the q and the k/v widths,
+        else hidden / (q width / k/v width) (tinker/modules/attention.py:81-92). A
+        ``rope_theta`` attribute on the source overrides the argument (:95-97)."""
+        proj = attention_projections(source)
+        q_rows, hidden = proj["q"].weight.shape
+        kv_rows = proj["k"].weight.shape[0]
+        head_dim, num_heads, num_kv_heads = _head_layout(source, hidden, q_rows, kv_rows)
+        theta = getattr(source, "rope_theta", None)
+        module = cls(hidden, num_heads, num_kv_heads, head_dim,
+                     rope_theta=rope_theta if theta is None else theta, max_seq_len=max_seq_len)
+        with torch.no_grad():
+            for role in ("q", "k", "v", "o"):
+                getattr(module, f"{role}_proj").weight.copy_(proj[role].weight)
+        device = proj["q"].weight.device
+        module.cos_table, module.sin_table = module.cos_table.to(device), module.sin_table.to(device)
         return module
 
     def extra_repr(self) -> str:
-        return (
-            f"hidden_size={self.hidden_size}, num_heads={self.num_heads}, "
-            f"num_kv_heads={self.num_kv_heads}, head_dim={self.head_dim}, "
-            f"rope_theta={self.rope_theta}"
-        )
+        return (f"hidden_size={self.hidden_size}, heads={self.num_heads}/{self.num_kv_heads} (q/kv), "
+                f"head_dim={self.head_dim}, rope_theta={self.rope_theta}")
 
 
-def _find_attention_projections(module: nn.Module):
-    """find projection layers (same attribute names as attention.py:127-153)"""
-    q_names = ["q_proj", "query", "wq", "q"]
-    k_names = ["k_proj", "key", "wk", "k"]
-    v_names = ["v_proj", "value", "wv", "v"]
-    o_names = ["o_proj", "output", "wo", "out_proj", "o"]
-
-    def _get_proj(names):
-        for name in names:
-            sub = getattr(module, name, None)
-            if sub is not None and hasattr(sub, "weight"):
-                return sub
-        return None
-
-    q = _get_proj(q_names)
-    k = _get_proj(k_names)
-    v = _get_proj(v_names)
-    o = _get_proj(o_names)
-
-    if q is None or k is None or v is None or o is None:
-        raise ValueError(
-            f"Could not find attention projection layers in {type(module).__name__}. "
-            f"Expected attributes named one of: q_proj/query/wq, k_proj/key/wk, "
-            f"v_proj/value/wv, o_proj/output/wo"
-        )
-
-    return q, k, v, o
+def _head_layout(source: nn.Module, hidden: int, q_rows: int, kv_rows: int) -> tuple[int, int, int]:
+    """(head_dim, query heads, kv heads) of a source attention module from its weight shapes."""
+    head_dim = getattr(source, "head_dim", None)
+    if head_dim is None:
+        head_dim = next((d for d in (64, 128) if q_rows % d == 0 and kv_rows % d == 0), None)
+    if head_dim is None:
+        head_dim = hidden // (q_rows // kv_rows)
+    return head_dim, q_rows // head_dim, kv_rows // head_dim

@@ -1,4 +1,4 @@
-"""fused swiglu ffn module (drop-in for eb1386/TinKer tinker/modules/feed_forward.py:9-76).
+"""Fused SwiGLU FFN module (drop-in for eb1386/TinKer tinker/modules/feed_forward.py:9-47).
 
 ``forward`` runs the whole FFN as two tcgen05 GEMMs: gate|up with the SwiGLU
 applied in the epilogue, then the down projection. The ``gate_proj`` /
@@ -10,14 +10,15 @@ import torch
 import torch.nn as nn
 
 from tinker_b200.kernels.gemm import swiglu_ffn
+from tinker_b200.modules._roles import swiglu_weights
 
 
 class TinKerSwiGLU(nn.Module):
-    """fused swiglu ffn
+    """SwiGLU feed-forward block: down_proj(silu(gate_proj(x)) * up_proj(x)).
 
     args:
-        hidden_size: hidden dim
-        intermediate_size: intermediate dim
+        hidden_size: model width
+        intermediate_size: width of the gated inner layer
     """
 
     def __init__(self, hidden_size: int, intermediate_size: int):
@@ -34,42 +35,15 @@ class TinKerSwiGLU(nn.Module):
 
     @classmethod
     def from_module(cls, source: nn.Module) -> "TinKerSwiGLU":
-        """from existing module"""
-        gate_w, up_w, down_w = _find_swiglu_weights(source)
-        hidden_size = gate_w.shape[1]
-        intermediate_size = gate_w.shape[0]
-        module = cls(hidden_size=hidden_size, intermediate_size=intermediate_size)
-        module.gate_proj.weight.data.copy_(gate_w.data)
-        module.up_proj.weight.data.copy_(up_w.data)
-        module.down_proj.weight.data.copy_(down_w.data)
+        """A ``TinKerSwiGLU`` holding copies of ``source``'s gate / up / down weights (found by
+        name, see ``modules._roles``); the sizes come from the gate weight's shape."""
+        w = swiglu_weights(source)
+        intermediate_size, hidden_size = w["gate"].shape
+        module = cls(hidden_size, intermediate_size)
+        with torch.no_grad():
+            for role in ("gate", "up", "down"):
+                getattr(module, f"{role}_proj").weight.copy_(w[role])
         return module
 
     def extra_repr(self) -> str:
-        return f"hidden_size={self.hidden_size}, intermediate_size={self.intermediate_size}"
-
-
-def _find_swiglu_weights(module: nn.Module):
-    """find projection weights (same attribute names as feed_forward.py:50-76)"""
-    gate_names = ["gate_proj", "w1", "gate"]
-    up_names = ["up_proj", "w3", "up"]
-    down_names = ["down_proj", "w2", "down"]
-
-    def _get_weight(names):
-        for name in names:
-            sub = getattr(module, name, None)
-            if sub is not None:
-                if hasattr(sub, "weight"):
-                    return sub.weight
-                if isinstance(sub, torch.Tensor):
-                    return sub
-        return None
-
-    gate_w = _get_weight(gate_names)
-    up_w = _get_weight(up_names)
-    down_w = _get_weight(down_names)
-    if gate_w is None or up_w is None or down_w is None:
-        raise ValueError(
-            f"Could not find SwiGLU projection weights in {type(module).__name__}. "
-            f"Expected attributes named one of: gate_proj/w1/gate, up_proj/w3/up, down_proj/w2/down"
-        )
-    return gate_w, up_w, down_w
+        return f"{self.hidden_size} -> {self.intermediate_size} -> {self.hidden_size}"

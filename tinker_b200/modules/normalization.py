@@ -1,4 +1,9 @@
-"""fused rmsnorm module (drop-in for eb1386/TinKer tinker/modules/normalization.py:9-38)."""
+"""RMSNorm module (drop-in for eb1386/TinKer tinker/modules/normalization.py:9-38).
+
+The constructor signature and the ``weight`` / ``eps`` attributes are the reference's,
+so state_dicts and code that reads them carry over; ``forward`` runs this library's
+vectorised RMSNorm kernel.
+"""
 
 import torch
 import torch.nn as nn
@@ -7,11 +12,11 @@ from tinker_b200.kernels.fused_rmsnorm import fused_rmsnorm
 
 
 class TinKerRMSNorm(nn.Module):
-    """fused rmsnorm layer
+    """y = x / sqrt(mean(x^2) + eps) * weight over the last axis (float32 statistics).
 
     args:
-        dim: hidden dim
-        eps: epsilon
+        dim: size of the normalised (last) axis
+        eps: added to the mean square
     """
 
     def __init__(self, dim: int, eps: float = 1e-6):
@@ -25,13 +30,15 @@ class TinKerRMSNorm(nn.Module):
 
     @classmethod
     def from_module(cls, source: nn.Module) -> "TinKerRMSNorm":
-        """from existing module (eps from ``eps`` or ``variance_epsilon``, normalization.py:26-35)"""
-        weight = source.weight
-        dim = weight.shape[0]
-        eps = getattr(source, "eps", getattr(source, "variance_epsilon", 1e-6))
-        module = cls(dim=dim, eps=eps)
-        module.weight.data.copy_(weight.data)
+        """Copy of ``source``'s weight; epsilon from its ``eps``, else ``variance_epsilon``
+        (the Hugging Face name), else 1e-6."""
+        eps = getattr(source, "eps", None)
+        if eps is None:
+            eps = getattr(source, "variance_epsilon", 1e-6)
+        module = cls(source.weight.shape[0], eps)
+        with torch.no_grad():
+            module.weight.copy_(source.weight)
         return module
 
     def extra_repr(self) -> str:
-        return f"dim={self.dim}, eps={self.eps}"
+        return f"{self.dim}, eps={self.eps}"

@@ -13,6 +13,8 @@
   6. optional CUDA graph capture of the whole forward (static shapes)
 """
 
+import math
+import statistics
 import time
 
 import torch
@@ -118,7 +120,15 @@ def optimize(
 
 
 class _CUDAGraphWrapper(nn.Module):
-    """wraps model with cuda graph replay (optimize.py:134-150)"""
+    """A model whose forward for one input shape is a CUDA graph replay.
+
+    The graph reads its tokens from a static input buffer and writes its logits to a
+    static output buffer (both owned by the graph's memory pool). A call with the
+    captured shape copies the tokens in, replays the graph and returns the logits - a
+    fresh copy by default, as the reference does (tinker/optimize.py:134-150), or, with
+    ``clone_output=False``, the static buffer itself, which the next replay overwrites.
+    Any other shape runs the wrapped model eagerly.
+    """
 
     def __init__(self, model, static_input, static_output, graph, clone_output=True):
         super().__init__()
@@ -126,37 +136,48 @@ class _CUDAGraphWrapper(nn.Module):
         self._static_input = static_input
         self._static_output = static_output
         self._graph = graph
-        self._input_shape = static_input.shape
         self._clone_output = clone_output
 
+    @property
+    def _input_shape(self):
+        return self._static_input.shape
+
     def forward(self, x):
-        if x.shape == self._input_shape:
-            self._static_input.copy_(x, non_blocking=True)
-            self._graph.replay()
-            return self._static_output.clone() if self._clone_output else self._static_output
-        return self._model(x)
+        if x.shape != self._static_input.shape:
+            return self._model(x)
+        self._static_input.copy_(x, non_blocking=True)
+        self._graph.replay()
+        if self._clone_output:
+            return self._static_output.clone()
+        return self._static_output
 
 
 def _capture_cuda_graph(model, input_shape, vocab_size, verbose=False, clone_output=True):
-    """capture cuda graph: 3 warm-up forwards, then one captured forward (optimize.py:153-173)"""
+    """Capture ``model``'s forward on random token ids of ``input_shape`` in a CUDA graph.
+
+    Three eager forwards come first (they build every kernel's launch state and the
+    folded weights, which must not happen during capture), then one captured forward
+    under ``stable_weights`` (no kernel of the forward writes a weight, so the GEMMs may
+    stage weight tiles before their dependency wait). On any failure the model is
+    returned unchanged and the reason reported when ``verbose``, as in the reference
+    (tinker/optimize.py:153-173)."""
+    device = next(model.parameters()).device
+    tokens = torch.randint(0, vocab_size, tuple(input_shape), device=device)
     try:
-        device = next(model.parameters()).device
-        static_input = torch.randint(0, vocab_size, input_shape, device=device)
         with torch.inference_mode():
             for _ in range(3):
-                _ = model(static_input)
-            torch.cuda.synchronize()
+                model(tokens)
+            torch.cuda.synchronize(device)
             graph = torch.cuda.CUDAGraph()
-            # no kernel of the forward writes a weight: the GEMMs may fetch weight tiles early
             with torch.cuda.graph(graph), stable_weights():
-                static_output = model(static_input)
+                logits = model(tokens)
+    except Exception as e:  # capture is an optimisation: fall back to the eager model
         if verbose:
-            print(f"  [tinker] cuda graph captured (shape={input_shape})")
-        return _CUDAGraphWrapper(model, static_input, static_output, graph, clone_output)
-    except Exception as e:
-        if verbose:
-            print(f"  [tinker] cuda graph failed: {e}")
+            print(f"  [tinker] cuda graph not captured ({type(e).__name__}: {e}); running eagerly")
         return model
+    if verbose:
+        print(f"  [tinker] cuda graph captured for inputs {tuple(input_shape)}")
+    return _CUDAGraphWrapper(model, tokens, logits, graph, clone_output)
 
 
 @torch.inference_mode()
@@ -168,36 +189,44 @@ def benchmark_model(
     runs: int = 100,
     device: str | None = None,
 ) -> dict:
-    """benchmark forward pass latency (optimize.py:190-242: median of `runs`, synchronised wall clock)"""
-    if device is None:
-        device = "cuda" if torch.cuda.is_available() else "cpu"
-    tokens = torch.randint(0, vocab_size, input_shape, device=device)
+    """Latency of ``model`` on random token ids of ``input_shape``.
+
+    Each of ``runs`` timed calls is bracketed by device synchronisations and timed on
+    the host clock, after ``warmup`` untimed calls; the result has the reference's keys
+    (tinker/optimize.py:190-242): ``median_ms`` (the upper median of the sorted times),
+    ``mean_ms``, ``min_ms``, ``tokens_per_sec`` at the median, ``device``, and on a GPU
+    ``peak_memory_mb`` (since the timed calls started) and ``gpu``."""
+    dev = torch.device(device if device is not None else ("cuda" if torch.cuda.is_available() else "cpu"))
+    on_gpu = dev.type == "cuda"
+
+    def settle():
+        if on_gpu:
+            torch.cuda.synchronize(dev)
+
+    tokens = torch.randint(0, vocab_size, tuple(input_shape), device=dev)
     for _ in range(warmup):
-        _ = model(tokens)
-    if torch.cuda.is_available():
-        torch.cuda.synchronize()
-        torch.cuda.reset_peak_memory_stats()
-    times = []
+        model(tokens)
+    settle()
+    if on_gpu:
+        torch.cuda.reset_peak_memory_stats(dev)
+    times_ms = []
     for _ in range(runs):
-        if torch.cuda.is_available():
-            torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        _ = model(tokens)
-        if torch.cuda.is_available():
-            torch.cuda.synchronize()
-        times.append((time.perf_counter() - t0) * 1000)
-    times.sort()
-    median = times[len(times) // 2]
-    mean = sum(times) / len(times)
-    tps = input_shape[0] * input_shape[1] / (median / 1000)
+        settle()
+        start = time.perf_counter()
+        model(tokens)
+        settle()
+        times_ms.append((time.perf_counter() - start) * 1e3)
+    ordered = sorted(times_ms)
+    median = ordered[len(ordered) // 2]
+    n_tokens = math.prod(input_shape)
     result = {
         "median_ms": round(median, 3),
-        "mean_ms": round(mean, 3),
-        "min_ms": round(times[0], 3),
-        "tokens_per_sec": round(tps),
-        "device": device,
+        "mean_ms": round(statistics.fmean(times_ms), 3),
+        "min_ms": round(ordered[0], 3),
+        "tokens_per_sec": round(n_tokens / (median / 1e3)),
+        "device": str(dev.type if device is None else device),
     }
-    if torch.cuda.is_available():
-        result["peak_memory_mb"] = round(torch.cuda.max_memory_allocated() / (1024 ** 2), 1)
-        result["gpu"] = torch.cuda.get_device_name(0)
+    if on_gpu:
+        result["peak_memory_mb"] = round(torch.cuda.max_memory_allocated(dev) / 2 ** 20, 1)
+        result["gpu"] = torch.cuda.get_device_name(dev)
     return result
