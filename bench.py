@@ -76,7 +76,8 @@ def _peaks():
 
 
 # ------------------------------------------------------------------------------------
-# CPU side: the reference's fp32 eager forward restated in numpy (oracle/)
+# CPU side: the reference's own fp32 eager forward (its blocks, carried in oracle/torch_model.py)
+# timed on the host cores; its logits are also the parity reference for the timed graph
 # ------------------------------------------------------------------------------------
 def _blas_threads() -> int:
     try:
@@ -89,80 +90,128 @@ def _blas_threads() -> int:
     return os.cpu_count() or 1
 
 
-def _use_all_host_threads():
-    """BLAS may inherit OMP_NUM_THREADS=1 from torchrun; the CPU baseline uses every core."""
+def _use_all_host_threads() -> int:
+    """torchrun exports OMP_NUM_THREADS=1; the CPU baseline uses every core of the host."""
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
     try:
         from threadpoolctl import threadpool_limits
-        threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+        threadpool_limits(limits=n, user_api="blas")
     except Exception:
         pass
+    return torch.get_num_threads()
 
 
-def _oracle_setup(cfg, seed=0):
-    import numpy as np
+def _reference_cpu_model(cfg, seed=0):
+    """The reference's unpatched fp32 eager model (oracle/torch_model.py) with the seeded weights."""
+    from oracle.torch_model import build_model as build_reference
+    return build_reference(cfg, seed=seed)
+
+
+def _reference_forward(model, tokens, layers=None):
+    """The reference model's forward, optionally over its first ``layers`` blocks only (a bounded
+    CPU sample; embedding, final norm and head always run)."""
+    x = model.embedding(tokens)
+    for blk in model.layers[:layers]:
+        x = blk(x)
+    return model.output(model.norm(x))
+
+
+def cpu_reference_timer(cfg, tokens, budget_s: float = 20.0, min_runs: int = 10, warmup: int = 3):
+    """Median ms of the reference's fp32 eager forward on all host threads (warm-up, then
+    min_runs..as many as fit in budget_s), its logits, and the thread count."""
+    import torch
+    threads = _use_all_host_threads()
+    model = _reference_cpu_model(cfg)
+    with torch.inference_mode():
+        for _ in range(warmup):
+            logits = _reference_forward(model, tokens)
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while len(times) < min_runs or (time.perf_counter() < t_end and len(times) < 100):
+            t = time.perf_counter()
+            _reference_forward(model, tokens)
+            times.append((time.perf_counter() - t) * 1e3)
+    return statistics.median(times), len(times), logits.float().numpy(), threads
+
+
+def numpy_port_timer(cfg, tokens, runs: int = 5):
+    """Secondary CPU figure: median ms of the numpy restatement (oracle/) of the same forward."""
     import oracle
     _use_all_host_threads()
     from bench_model import build_model
-    m = build_model(cfg, seed=seed)
-    w = {k: v.detach().float().numpy() for k, v in m.state_dict().items()}
+    w = {k: v.detach().float().numpy() for k, v in build_model(cfg, seed=0).state_dict().items()}
     ocfg = oracle.ModelConfig(**{f: getattr(cfg, f) for f in oracle.ModelConfig.__dataclass_fields__})
-    return oracle, w, ocfg, np
-
-
-def cpu_forward_timer(cfg, tokens, budget_s: float, max_runs: int):
-    """Median ms of the numpy fp32 forward over a bounded number of runs."""
-    oracle, w, ocfg, np = _oracle_setup(cfg)
     tok = tokens.numpy()
-    t0 = time.perf_counter()
-    oracle.forward_logits(w, tok, ocfg)  # warm-up
-    first = time.perf_counter() - t0
-    runs = max(1, min(max_runs, int(budget_s / max(first, 1e-3))))
+    oracle.forward_logits(w, tok, ocfg)
     times = []
     for _ in range(runs):
         t = time.perf_counter()
         oracle.forward_logits(w, tok, ocfg)
         times.append((time.perf_counter() - t) * 1e3)
-    return statistics.median(times), runs
+    return statistics.median(times)
+
+
+def logits_parity(ours, ref) -> dict:
+    """Max-abs error of half-precision logits against the fp32 reference, raw top-1 agreement,
+    and top-1 agreement over the positions whose fp32 top-1/top-2 gap exceeds twice the max-abs
+    error (random weights give near-ties that no half-precision forward resolves)."""
+    import numpy as np
+    ours = np.asarray(ours, dtype=np.float64).reshape(-1, ref.shape[-1])
+    ref = np.asarray(ref, dtype=np.float64).reshape(-1, ref.shape[-1])
+    err = np.abs(ours - ref)
+    top2 = np.sort(ref, axis=-1)[:, -2:]
+    gap = top2[:, 1] - top2[:, 0]
+    agree = ours.argmax(-1) == ref.argmax(-1)
+    clear = gap > 2 * err.max()
+    return {"max_abs": float(f"{err.max():.4g}"), "mean_abs": float(f"{err.mean():.4g}"),
+            "top1": round(float(agree.mean()), 5),
+            "top1_clear_margin": round(float(agree[clear].mean()), 5) if clear.any() else 1.0,
+            "positions": int(ref.shape[0]), "clear_positions": int(clear.sum())}
 
 
 def run_reference(args):
+    """``--impl reference``: the reference's CPU path - its unpatched fp32 eager forward - timed on
+    this host's cores, rank 0 only; each step one forward of the 268M decoder at batch 1 x seq 128
+    (fewer blocks, scaled, if a full forward would not fit the step budget)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU reference runs once, on rank 0
-    import numpy as np
-    import oracle
+    import torch
     from bench_model import LLAMA_268M, make_tokens
     cfg = LLAMA_268M
     tokens = make_tokens(cfg, 1, 128, seed=1)
-    oracle_mod, w, ocfg, _ = _oracle_setup(cfg)
-    tok = tokens.numpy()
-    # size each step so that the whole --warmup/--steps run stays within ~3 minutes
-    t = time.perf_counter()
-    oracle.forward_logits(w, tok, ocfg)
-    full_s = time.perf_counter() - t
-    budget = 180.0 / max(1, args.steps + args.warmup)
-    layers = cfg.num_layers
-    if full_s > budget:
-        layers = max(1, int(cfg.num_layers * budget / full_s))
-    for _ in range(args.warmup):
-        oracle.forward_logits(w, tok, ocfg, num_layers=layers)
-    times = []
-    for _ in range(args.steps):
+    threads = _use_all_host_threads()
+    model = _reference_cpu_model(cfg)
+    with torch.inference_mode():
         t = time.perf_counter()
-        oracle.forward_logits(w, tok, ocfg, num_layers=layers)
-        times.append((time.perf_counter() - t) * 1e3 * cfg.num_layers / layers)
+        _reference_forward(model, tokens)
+        full_s = time.perf_counter() - t
+        budget = 180.0 / max(1, args.steps + args.warmup)  # the whole run within ~3 minutes
+        layers = cfg.num_layers
+        if full_s > budget:
+            layers = max(1, int(cfg.num_layers * budget / full_s))
+        for _ in range(args.warmup):
+            _reference_forward(model, tokens, layers)
+        times = []
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            _reference_forward(model, tokens, layers)
+            times.append((time.perf_counter() - t) * 1e3 * cfg.num_layers / layers)
     ms = statistics.median(times)
-    sample = ("full 268M fp32 forward, batch 1 x seq 128, numpy (BLAS) restatement of the reference's eager path"
-              if layers == cfg.num_layers else
-              f"{layers} of 18 decoder layers + embedding/head per step, scaled x{cfg.num_layers / layers:.2f} to a "
-              "full 268M fp32 forward, batch 1 x seq 128, numpy restatement of the reference's eager path")
-    cores = _blas_threads()
+    what = ("the reference's unpatched fp32 eager forward (benchmarks/bench_e2e.py blocks + embedding/head, "
+            "torch CPU ops), 268M decoder, batch 1 x seq 128")
+    sample = what if layers == cfg.num_layers else \
+        f"{layers} of 18 blocks + embedding/head per step, scaled x{cfg.num_layers / layers:.2f}: {what}"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic: seeded N(0,0.02) weights, uniform token ids",
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic: seeded N(0,0.02) weights, uniform token ids",
         "config": {"workload": "llama268m-b1s128", "global_batch": 1, "seq_len": 128, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": threads, "kind": "reference",
+                         "sample": sample},
         "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -596,6 +645,7 @@ def run_ours(args):
     ms_mean, ms_median = _time_replays(graph, args.steps)
     _barrier(world)
     ms = _max_over_ranks(ms_mean, world, dev)
+    graph_logits = model._static_output.float().cpu().numpy()  # the timed replays' own output
 
     # ---- end to end through the public call -----------------------------------------------------
     tok_host = tokens.pin_memory()
@@ -632,6 +682,7 @@ def run_ours(args):
 
     # ---- batched Qwen-shaped prefill, sequences split across ranks ---------------------------------
     batched = None
+    batched_rows = None  # (tokens, logits) of the first and last sequence of the timed graph, for parity
     if not args.no_batched:
         qcfg = QWEN25_05B_SHAPED
         per_rank = 64 // world
@@ -648,6 +699,8 @@ def run_ours(args):
         qms, _ = _time_replays(qm._graph, args.batched_steps)
         _barrier(world)
         qms = _max_over_ranks(qms, world, dev)
+        pick = [0, per_rank - 1]
+        batched_rows = (qtok[pick], qm._static_output[pick].float().cpu().numpy())
         flops = 2 * 64 * 512 * (qcfg.num_params() - qcfg.vocab_size * qcfg.hidden_size) \
             + 2 * 64 * 512 * qcfg.vocab_size * qcfg.hidden_size \
             + qcfg.num_layers * 2 * 2 * 64 * qcfg.num_heads * qcfg.head_dim * 512 * 512 // 2
@@ -670,12 +723,26 @@ def run_ours(args):
             d_["n_gpus"] = world
         decode.append(_kv_attention_bench(dev, peaks, peak_note))
 
-    # ---- CPU baseline (rank 0 at N=1) ----------------------------------------------------------------
+    # ---- CPU baseline (rank 0 at N=1): the reference's fp32 eager forward; its logits are the
+    # parity reference for the timed graph's own output ---------------------------------------------
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_ms, runs = cpu_forward_timer(cfg, tokens, budget_s=20.0, max_runs=30)
-        cpu = {"value": round(cpu_ms, 3), "unit": "ms", "cores": _blas_threads(), "kind": "port",
-               "sample": f"{runs} full 268M fp32 forwards (b1 s128) of the numpy restatement of the reference's eager path"}
+        cpu_ms, runs, ref_logits, threads = cpu_reference_timer(cfg, tokens)
+        port_ms = numpy_port_timer(cfg, tokens)
+        cpu = {"value": round(cpu_ms, 3), "unit": "ms", "cores": threads, "kind": "reference",
+               "sample": f"median of {runs} full 268M fp32 forwards (b1 s128) of the reference's unpatched eager "
+                         "model (its benchmarks/bench_e2e.py blocks + embedding/head, torch CPU ops) after 3 warm-ups",
+               "numpy_port_ms": round(port_ms, 3)}
+        parity = {"llama268m_b1s128_fp16_graph": {**logits_parity(graph_logits, ref_logits),
+                                                  "vs": "reference fp32 eager forward (CPU), same weights/tokens"}}
+        if batched_rows is not None:
+            qcfg = QWEN25_05B_SHAPED
+            qref = _reference_forward(_reference_cpu_model(qcfg), batched_rows[0])
+            parity["qwen_shaped_b64s512_bf16_graph"] = {
+                **logits_parity(batched_rows[1], qref.float().numpy()),
+                "vs": "reference fp32 eager forward (CPU) of the first and last of the 64 sequences"}
+            del qref
 
     if rank == 0:
         line = {
@@ -694,7 +761,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": 128 * cfg.vocab_size * 2},
             "roofline": roof, "roofline_forward": roof_fwd, "kernels": table,
             "gpu_launches": launches_per_fwd * args.steps, "gpu_launches_per_fwd": launches_per_fwd,
-            "clocks": clocks, "cpu_baseline": cpu, "batched": batched, "decode": decode,
+            "clocks": clocks, "cpu_baseline": cpu, "parity": parity, "batched": batched, "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

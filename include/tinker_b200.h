@@ -217,6 +217,14 @@ TK_API int tk_decode_step_setup(const tk_step_layer* layers, int num_layers, int
                                 const void* final_norm_weight, float final_eps, int dtype, void* scratch,
                                 int64_t scratch_bytes);
 TK_API int tk_decode_step(void* x, void* y, void* scratch, void* stream);
+/*
+ * Test hook for the failure path (no counterpart in the reference): with cta >= 0, CTA `cta` of
+ * the next tk_decode_step launches on `scratch` does not arrive at the step's first grid
+ * barrier, so every CTA's bounded wait there runs out after TK_WAIT_LIMIT_NS (2 s): the step
+ * records device error 1 (tk_device_error), every CTA returns and the outputs are invalid;
+ * cta = -1 (the default after tk_decode_step_setup) turns it off. Nothing is faulted.
+ */
+TK_API int tk_decode_step_withhold_arrival(void* scratch, int cta);
 /* Forget the plan tk_decode_step_setup stored for `scratch` (before freeing it). */
 TK_API int tk_decode_step_release(void* scratch);
 

@@ -21,7 +21,10 @@ pytestmark = pytest.mark.gpu
 TOL = 5e-3
 
 
-def _run(B, S, hq, hkv, d, dtype, start_pos=0, theta=1e4, table_dtype=torch.float32, seed=42, fused=False):
+def _run(B, S, hq, hkv, d, dtype, start_pos=0, theta=1e4, table_dtype=torch.float32, seed=42, fused=False,
+         check=None):
+    """Kernel output and oracle output; with ``check`` (batch indices) the kernel runs on the
+    whole batch and both are returned for those sequences only (sequences are independent)."""
     from tinker_b200.kernels.fused_attention import fused_attention, precompute_rope_tables
     g = torch.Generator(device="cuda").manual_seed(seed)
     if fused:
@@ -33,6 +36,8 @@ def _run(B, S, hq, hkv, d, dtype, start_pos=0, theta=1e4, table_dtype=torch.floa
         v = torch.randn(B, S, hkv * d, device="cuda", generator=g).to(dtype)
     cos, sin = precompute_rope_tables(d, max(S + start_pos, 256), theta, device="cuda", dtype=table_dtype)
     out = fused_attention(q, k, v, cos, sin, hq, hkv, d, start_pos=start_pos)
+    if check is not None:
+        out, q, k, v = out[check], q[check], k[check], v[check]
     ref = oracle.attention(np32(q), np32(k), np32(v), np32(cos), np32(sin), hq, hkv, d, start_pos,
                            io_dtype=NP_NAME[dtype])
     return out, ref
@@ -59,6 +64,22 @@ def test_reference_configs_bf16(hidden, hq, hkv, d, S, B):
 def test_sweep(dt, B, S, d, hq, hkv):
     require_b200()
     out, ref = _run(B, S, hq, hkv, d, DTYPES[dt], seed=B * S + d + hkv)
+    assert rel_err(np32(out), ref) <= TOL
+
+
+# the sweep's batch-32 and long-sequence shapes (the reference benchmarks them,
+# tinker/kernels/fused_attention.py:195-231 on these sizes): the kernel runs on the whole
+# batch, the oracle checks the first and the last sequence
+LARGE = [(32, 128, 64, 16, 4), (32, 512, 64, 16, 4), (32, 512, 128, 16, 4), (32, 512, 64, 16, 1),
+         (8, 2048, 64, 16, 4), (8, 2048, 128, 16, 4), (8, 2048, 64, 16, 16), (8, 2048, 128, 16, 1),
+         (32, 2048, 64, 16, 4)]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("B, S, d, hq, hkv", LARGE)
+def test_sweep_large(dt, B, S, d, hq, hkv):
+    require_b200()
+    out, ref = _run(B, S, hq, hkv, d, DTYPES[dt], seed=B * S + d + hkv + 1, check=[0, B - 1])
     assert rel_err(np32(out), ref) <= TOL
 
 

@@ -341,3 +341,44 @@ def test_fused_step_stops_on_device_error():
         torch.cuda.synchronize()
     assert _lib.device_error(clear=True) == 0
     assert torch.isfinite(lg.float()).all()
+
+
+@pytest.mark.gpu
+def test_fused_step_bounded_wait_runs_out_and_recovers():
+    """A grid-barrier wait that nothing completes: with the test hook one CTA of the one-kernel
+    step withholds its arrival at the first barrier, so every CTA's wait there runs out after
+    the 2 s limit. The launch returns, device error 1 (timeout) is recorded, and after clearing
+    it the next step on the same decoder is finite and equals the per-block step."""
+    require_b200()
+    import time
+    import tinker_b200
+    from tinker_b200 import _lib
+    from bench_model import make_tokens
+    cfg, _, model = _decoder(2)
+    tokens = make_tokens(cfg, 1, 12, seed=13).cuda()
+    ref = tinker_b200.CachedDecoder(model, batch_size=1, capacity=16, cuda_graph=False, fused_step=False)
+    dec = tinker_b200.CachedDecoder(model, batch_size=1, capacity=16, cuda_graph=False, fused_step=True)
+    _lib.device_error(clear=True)
+    lib = _lib.lib()
+    with torch.inference_mode():
+        ref.prefill(tokens[:, :10])
+        want = ref.decode(tokens[:, 10]).float()
+        dec.prefill(tokens[:, :10])
+        dec._setup_step()
+        dec.cache.position.fill_(10)
+        scratch = dec._step_scratch.data_ptr()
+        _lib.check(lib.tk_decode_step_withhold_arrival(scratch, 3), "tk_decode_step_withhold_arrival")
+        t0 = time.perf_counter()
+        dec._fused_forward(tokens[:, 10:11])
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+        assert _lib.device_error(clear=True) == 1  # TK_DEVERR_TIMEOUT
+        assert 1.5 < waited < 30, waited
+        _lib.check(lib.tk_decode_step_withhold_arrival(scratch, -1), "tk_decode_step_withhold_arrival")
+        got = dec.decode(tokens[:, 10]).float()  # position 10 again (the failed step wrote no cache row)
+        torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
+    assert torch.isfinite(got).all()
+    assert (got - want).abs().max().item() <= 2e-2 * max(1.0, want.abs().max().item())
+    with pytest.raises(RuntimeError):
+        _lib.check(lib.tk_decode_step_withhold_arrival(scratch, -2), "tk_decode_step_withhold_arrival")

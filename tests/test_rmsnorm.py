@@ -1,7 +1,7 @@
 """RMSNorm parity: CUDA kernel (through the C ABI) vs the numpy oracle.
 
 Cases: the reference's own test shapes (tests/test_rmsnorm.py:21-28 of
-eb1386/TinKer), the kernel sweep rows {128, 4096} x hidden {1024, 2048, 4096}
+eb1386/TinKer), the kernel sweep rows {128, 4096, 65536} x hidden {1024, 2048, 4096}
 in fp16 and bf16, fp32, odd and unaligned dims, strided rows and the fused
 residual variant. Bar: the kernel output equals the oracle's (float32 math,
 one rounding) to within one ulp of the output dtype everywhere, and the
@@ -41,7 +41,7 @@ def test_reference_shapes_bf16(dim, seq, batch):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-@pytest.mark.parametrize("rows", [128, 4096])
+@pytest.mark.parametrize("rows", [128, 4096, 65536])
 @pytest.mark.parametrize("hidden", [1024, 2048, 4096])
 def test_sweep(dt, rows, hidden):
     require_b200()

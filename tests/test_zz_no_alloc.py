@@ -7,8 +7,10 @@ milliseconds). For them tk_swiglu_ffn_noalloc keeps the [m, f] activation in a
 fixed 8 MiB array inside the library. This test calls it through the C ABI,
 twice in a row with different inputs (the array keeps the previous call's
 contents), and checks each result against tk_swiglu_ffn with a caller-provided
-scratch buffer, within the FFN tolerance of the other tests (<= 1e-3 norm-wise
-relative for fp16). It also checks that sizes beyond the array are rejected.
+scratch buffer and against the float64 FFN on the host, within the FFN tolerance
+of the other tests (<= 1e-3 norm-wise relative for fp16), at the 268M decoder's
+shape, at a 4-row batch (the few-row kernels) and at m * f * 2 exactly equal to
+the array's 8 MiB. It also checks that sizes beyond the array are rejected.
 The file is named to be collected last.
 """
 
@@ -28,12 +30,25 @@ def _call(fn, *args):
         raise RuntimeError(_lib.last_error())
 
 
-def test_noalloc_ffn_matches_scratch_ffn_twice():
+def _ffn_oracle(x, wg, wu, wd):
+    """The FFN in float64 on the host: down(silu(x gate^T) * (x up^T)) (oracle.swiglu's arithmetic)."""
+    xx = np32(x).astype(np.float64)
+    a = xx @ np32(wg).astype(np.float64).T
+    b = xx @ np32(wu).astype(np.float64).T
+    return (a / (1.0 + np.exp(-a)) * b) @ np32(wd).astype(np.float64).T
+
+
+# (m, hidden, f): the 268M decoder's FFN at batch 1 x seq 128; a decode-sized batch that takes
+# the few-row (GEMV) kernels; and m * f * 2 exactly the 8 MiB of the array
+CASES = [(128, 1024, 2816), (4, 1024, 2816), (1024, 1024, 4096)]
+
+
+@pytest.mark.parametrize("m, hidden, f", CASES)
+def test_noalloc_ffn_matches_scratch_ffn_twice(m, hidden, f):
     require_b200()
     from tinker_b200 import _lib
     lib = _lib.lib()
-    torch.manual_seed(11)
-    m, hidden, f = 128, 1024, 2816  # the 268M decoder's FFN at batch 1 x seq 128
+    torch.manual_seed(11 + m)
     dev = torch.device("cuda", 0)
     wg = (0.02 * torch.randn(f, hidden, device=dev)).half()
     wu = (0.02 * torch.randn(f, hidden, device=dev)).half()
@@ -51,8 +66,11 @@ def test_noalloc_ffn_matches_scratch_ffn_twice():
         torch.cuda.synchronize()
         o, r = np32(out), np32(ref)
         assert np.isfinite(o).all(), f"call {call}: non-finite output"
+        # same result as the entry point with a caller-provided buffer ...
         assert rel_err(o, r) <= 1e-3, f"call {call}"
         np.testing.assert_allclose(o, r, rtol=2e-3, atol=2e-3 * np.abs(r).max())
+        # ... and as the float64 FFN (the FFN bar of the other tests: <= 1e-3 for fp16)
+        assert rel_err(o, _ffn_oracle(x, wg, wu, wd)) <= 1e-3, f"call {call}"
 
 
 def test_noalloc_ffn_rejects_sizes_beyond_its_array():

@@ -71,6 +71,7 @@ SIGNATURES = {
                              _P, _I64],
     "tk_decode_step": [_P, _P, _P, _P],
     "tk_decode_step_release": [_P],
+    "tk_decode_step_withhold_arrival": [_P, _I],
 }
 
 # entry points whose return value is not a status

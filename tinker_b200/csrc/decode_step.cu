@@ -60,6 +60,7 @@ struct Params {
   float* ssq_x;   // [hidden / COLS, m]
   float* ssq_h;   // [hidden / COLS, m]
   unsigned* bar;  // arrival counter (zeroed before each launch)
+  int withhold_cta;  // test hook: this CTA does not arrive at the first grid barrier (-1: none)
 };
 
 // ---- grid barrier ---------------------------------------------------------------------------
@@ -75,7 +76,9 @@ __device__ __forceinline__ int device_error_now() {
 // Every CTA arrives; returns false (in every thread of the CTA) when the step must stop. The
 // counter only grows during a launch (zeroed before it): barrier k waits for k * gridDim.x
 // arrivals. `k` counts this CTA's barriers (the same sequence in every CTA).
-__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned& k) {
+// `arrive` false (only the tk_decode_step_withhold_arrival test hook) makes the CTA wait without
+// arriving, so that every CTA's bounded wait runs out.
+__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned& k, bool arrive = true) {
   __shared__ int s_ok;
   __syncthreads();
   ++k;
@@ -83,7 +86,7 @@ __device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned& k) {
     int ok = device_error_now() == 0;
     if (ok) {
       __threadfence();  // publish this CTA's writes
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+      if (arrive) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
       const unsigned target = k * gridDim.x;
       const uint64_t t0 = globaltimer();
       while (ld_acquire(bar) < target) {
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_step_kernel(const Params p)
     }
     p.ssq_x[static_cast<int64_t>(part) * m + row] = s;
   }
-  if (!grid_barrier(p.bar, nbar)) return;
+  if (!grid_barrier(p.bar, nbar, p.withhold_cta != static_cast<int>(blockIdx.x))) return;
 
   auto qkv_of = [&](const Layer& L) {
     return Product{p.x, L.wq, p.q_width, L.wk, p.kv_width, L.wv, p.q_width + 2 * p.kv_width, p.hidden,
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_step_kernel(const Params p)
     // q|k|v with the attention RMSNorm folded in; the cached keys/values of this CTA's attention
     // items go to L2 meanwhile
     {
-      const int kv_len = *kv.start_dev + 1;
+      const int kv_len = __ldcg(kv.start_dev) + 1;
       for (int item = blockIdx.x; item < p.kv_items; item += gridDim.x) {
         if (item % p.kv_chunks || kv_len < 1 || kv_len > kv.cap) continue;
         const int rest = item / p.kv_chunks;
@@ -443,11 +446,17 @@ Layout layout(int num_layers, int batch, int hidden, int num_heads, int num_kv_h
 template <int DT, int D, int R, int M>
 int launch(const Plan& pl, cudaStream_t st) {
   auto kern = decode_step_kernel<DT, D, R, M>;
-  static bool configured[64] = {};
-  static int per_sm[64] = {};
+  static std::mutex mu;
+  static int per_sm[64] = {};  // 0 until configured; written and read under mu
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
-  if (!configured[dev.device]) {
+  int resident = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    resident = per_sm[dev.device];
+  }
+  if (!resident) {
+    std::lock_guard<std::mutex> lock(mu);
     if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(pl.smem)),
                             "cudaFuncSetAttribute(decode_step)"))
@@ -458,12 +467,12 @@ int launch(const Plan& pl, cudaStream_t st) {
       return rc;
     if (n < 1) return set_error(TK_ERR_UNSUPPORTED, "decode_step: the kernel does not fit on an SM");
     per_sm[dev.device] = n;
-    configured[dev.device] = true;
+    resident = n;
   }
   if (int rc = check_cuda(cudaMemsetAsync(pl.p.bar, 0, 2 * sizeof(unsigned), st), "decode_step barrier reset"))
     return rc;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(dev.sm_count * per_sm[dev.device]);  // every CTA resident
+  cfg.gridDim = dim3(dev.sm_count * resident);  // every CTA resident
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
@@ -617,6 +626,7 @@ extern "C" int tk_decode_step_setup(const tk_step_layer* layers, int num_layers,
   p.ssq_x = reinterpret_cast<float*>(base + L.ssq_x);
   p.ssq_h = reinterpret_cast<float*>(base + L.ssq_h);
   p.bar = reinterpret_cast<unsigned*>(base + L.bar);
+  p.withhold_cta = -1;
   pl.dtype = dtype;
   pl.head_dim = head_dim;
   pl.rows_cta = kp.rows_cta;
@@ -643,6 +653,17 @@ extern "C" int tk_decode_step(void* x, void* y, void* scratch, void* stream) {
   if (pl.dtype == TK_F16)
     return pl.head_dim == 64 ? launch_r<TK_F16, 64>(pl, st) : launch_r<TK_F16, 128>(pl, st);
   return pl.head_dim == 64 ? launch_r<TK_BF16, 64>(pl, st) : launch_r<TK_BF16, 128>(pl, st);
+}
+
+extern "C" int tk_decode_step_withhold_arrival(void* scratch, int cta) {
+  using namespace tk;
+  std::lock_guard<std::mutex> lock(tk::step::g_mu);
+  auto it = tk::step::g_plans.find(scratch);
+  if (it == tk::step::g_plans.end())
+    return fail_invalid("decode_step: scratch was not prepared by tk_decode_step_setup");
+  if (cta < -1) return fail_invalid("decode_step_withhold_arrival: cta must be >= -1");
+  it->second.p.withhold_cta = cta;
+  return TK_OK;
 }
 
 extern "C" int tk_decode_step_release(void* scratch) {

@@ -13,16 +13,21 @@
 //  * The array holds TK_FFN_NOALLOC_SCRATCH_BYTES (8 MiB): m * f * 2 bytes must
 //    fit, otherwise the call returns TK_ERR_INVALID. Every GPU that loads the
 //    library keeps these 8 MiB until the process exits.
-//  * The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current) and caches it; make that
-//    first call before any stream capture starts.
+//  * The first call in each CUDA context looks up the array's device address
+//    (cudaGetSymbolAddress, with that context's device current) and caches it
+//    under the context's unique ID, so a context created later on the same
+//    device (after cudaDeviceReset, or a host's own non-primary context) gets
+//    its own lookup; make that first call before any stream capture starts.
 //  * All calls on a device share the one array, which keeps the last call's
 //    contents. Nothing in it has to start at zero: the gate|up kernel writes
 //    every element the down kernel then reads. Calls whose work overlaps on the
 //    GPU (e.g. on two streams at once) race on the array and must be ordered by
 //    the caller.
+#include <cuda.h>
+
 #include <cstdio>
 #include <mutex>
+#include <unordered_map>
 
 #include "tk_common.cuh"
 #include "tk_host.h"
@@ -32,8 +37,57 @@
 static __device__ __align__(256) unsigned char g_ffn_scratch[TK_FFN_NOALLOC_SCRATCH_BYTES];
 
 namespace {
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[64] = {};  // per-device address of g_ffn_scratch
+std::unordered_map<unsigned long long, void*> g_scratch_ptr;  // context ID -> address of g_ffn_scratch
+
+// The unique ID of the calling thread's current context (0 if there is none yet or the driver
+// cannot tell); IDs are never reused within a process, unlike context handles.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the scratch array in the current context.
+int scratch_address(void** out) {
+  using namespace tk;
+  unsigned long long id = current_context_id();
+  if (id) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    auto it = g_scratch_ptr.find(id);
+    if (it != g_scratch_ptr.end()) {
+      *out = it->second;
+      return TK_OK;
+    }
+  }
+  void* p = nullptr;  // this also makes the device's primary context current if none was
+  if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_ffn_scratch), "cudaGetSymbolAddress(scratch)")) return rc;
+  if (!id) id = current_context_id();
+  if (id) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    g_scratch_ptr[id] = p;
+  }
+  *out = p;
+  return TK_OK;
+}
 }  // namespace
 
 extern "C" int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
@@ -51,18 +105,7 @@ extern "C" int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const 
                   static_cast<unsigned long long>(need), TK_FFN_NOALLOC_SCRATCH_BYTES);
     return fail_invalid(buf);
   }
-  int dev = 0;
-  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
-  if (dev < 0 || dev >= 64) return set_error(TK_ERR_UNSUPPORTED, "swiglu_ffn_noalloc: device index out of range");
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
-      void* p = nullptr;
-      if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_ffn_scratch), "cudaGetSymbolAddress(scratch)")) return rc;
-      g_scratch_ptr[dev] = p;
-    }
-    scratch = g_scratch_ptr[dev];
-  }
+  if (int rc = scratch_address(&scratch)) return rc;
   return tk_swiglu_ffn(x, x_row_stride, w_gate, w_up, w_down, scratch, out, residual, m, hidden, f, dtype, stream);
 }

@@ -22,6 +22,7 @@
 #include <map>
 #include <mutex>
 #include <numeric>
+#include <string>
 #include <tuple>
 
 #include "tk_common.cuh"
@@ -881,6 +882,57 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ---------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------
+
+// Plan limits, checked on the host before every launch of the three GEMM kernels.
+// TMEM: a CTA's columns times the CTAs that can share an SM (by shared memory, threads
+// and registers) stay within the SM's 512 columns, so a tcgen05.alloc never waits for
+// columns held by another CTA - a CTA blocked in its alloc while its cluster peers wait
+// for it at a cluster barrier, and the columns' owners wait for theirs, would never
+// finish. Cached per (kernel, shared memory, device).
+template <typename... KArgs>
+static int check_tmem_residency(void (*kern)(KArgs...), int threads, size_t smem, uint32_t cols, const char* what) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, size_t, int>, int> cache;
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), smem, dev.device);
+  int resident = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) resident = it->second;
+  }
+  if (!resident) {
+    if (int rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, threads, smem),
+                            "cudaOccupancyMaxActiveBlocksPerMultiprocessor(gemm)"))
+      return rc;
+    if (resident < 1) return set_error(TK_ERR_UNSUPPORTED, std::string(what) + ": the plan does not fit on an SM");
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = resident;
+  }
+  if (static_cast<uint64_t>(resident) * cols > 512u)
+    return set_error(TK_ERR_UNSUPPORTED, std::string(what) + ": " + std::to_string(resident) +
+                                             " resident CTAs x " + std::to_string(cols) +
+                                             " TMEM columns exceed the SM's 512");
+  return TK_OK;
+}
+
+// Split-K plan limits: every CTA of a cluster accumulates at least one k-block (a CTA without
+// one would add an unwritten accumulator to the others), clusters of at most 8 CTAs (the
+// portable size), a ring that fits the barrier array, and shared memory within the device's
+// opt-in limit.
+static int check_splitk_plan(int split, int stages, int num_kb, size_t smem, size_t smem_cap) {
+  if (split < 1 || split > 8 || split > num_kb)
+    return set_error(TK_ERR_UNSUPPORTED, "gemm split-K plan: split " + std::to_string(split) + " for " +
+                                             std::to_string(num_kb) + " k-blocks (must be 1..min(8, k-blocks))");
+  if (stages < 1 || stages > SplitSmem<32>::MAX_STAGES)
+    return set_error(TK_ERR_UNSUPPORTED, "gemm split-K plan: " + std::to_string(stages) + " ring stages");
+  if (smem > smem_cap)
+    return set_error(TK_ERR_UNSUPPORTED, "gemm split-K plan: " + std::to_string(smem) +
+                                             " bytes of shared memory exceed the device limit");
+  return TK_OK;
+}
+
 template <int DT, int BN, int EPI, int STAGES>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& tb2,
            const Params& p, int ctas_per_sm, cudaStream_t st) {
@@ -895,6 +947,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1
       return rc;
     configured[dev.device] = true;
   }
+  if (int rc = check_tmem_residency(kern, THREADS, S::TOTAL, S::TMEM_COLS, "gemm_kernel")) return rc;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = std::max(1, std::min(tiles, dev.sm_count * ctas_per_sm));
   return launch_kernel(kern, dim3(grid), dim3(THREADS), S::TOTAL, st, 1, "gemm_kernel", ta, tb0, tb1, tb2, p);
@@ -927,6 +980,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
     if (int rc = check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "cudaOccupancyMaxActiveClusters")) return rc;
     max_pairs[dev.device] = std::max(1, n);
   }
+  if (int rc = check_tmem_residency(kern, PAIR_THREADS, S::TOTAL, S::TMEM_COLS, "gemm_pair_kernel")) return rc;
   const int tiles = p.m_tiles * p.n_tiles;
   const int pairs = std::max(1, std::min(tiles, max_pairs[dev.device]));
   return launch_kernel(kern, dim3(2 * pairs), dim3(PAIR_THREADS), S::TOTAL, st, 2, "gemm_pair_kernel", ta, tb0, tb1, tb2,
@@ -951,7 +1005,10 @@ int launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorM
       return rc;
     configured[dev.device] = true;
   }
-  return launch_kernel(kern, dim3(split, p.n_tiles, p.m_tiles), dim3(THREADS), S::total(split, stages), st, split,
+  const size_t smem = S::total(split, stages);
+  if (int rc = check_splitk_plan(split, stages, p.num_kb, smem, dev.smem_optin)) return rc;
+  if (int rc = check_tmem_residency(kern, THREADS, smem, S::TMEM_COLS, "gemm_splitk_kernel")) return rc;
+  return launch_kernel(kern, dim3(split, p.n_tiles, p.m_tiles), dim3(THREADS), smem, st, split,
                        "gemm_splitk_kernel", ta, tb0, tb1, tb2, p, split, stages);
 }
 

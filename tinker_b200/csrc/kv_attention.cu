@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(THREADS) kv_attention_kernel(const Params p) {
     // pull the first CHUNK_KEYS of this CTA's share into L2 while that kernel finishes (a hint
     // only, so a position that is about to change does no harm; longer ranges are left to the
     // cp.async pipeline, which a larger prefetch only competes with).
-    const int start = p.start_dev ? *p.start_dev : p.start_pos;
+    const int start = p.start_dev ? __ldcg(p.start_dev) : p.start_pos;  // L2: never a stale L1 line
     const int kv_len = start + p.seq;
     if (start > 0 && kv_len <= p.cap) {
       const int n_chunks = min(p.n_chunks, (kv_len + CHUNK_KEYS - 1) / CHUNK_KEYS);

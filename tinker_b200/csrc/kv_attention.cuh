@@ -161,7 +161,7 @@ __device__ __forceinline__ void kv_attention_item(const Params& p, int chunk, in
   int* last_s = reinterpret_cast<int*>(smem + S::FLAG_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int start = p.start_dev ? *p.start_dev : p.start_pos;
+  const int start = p.start_dev ? __ldcg(p.start_dev) : p.start_pos;  // the position may be fresh: read it from L2
   const int64_t end = static_cast<int64_t>(start) + p.seq;
   if (start < 0 || end > p.cap || end > p.table_rows) {
     if (threadIdx.x == 0 && report) record_device_error(TK_DEVERR_POSITION);
