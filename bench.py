@@ -52,9 +52,9 @@ def _args():
     ap.add_argument("--batched-steps", type=int, default=10)
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["forward", "gate_up_swiglu", "down_proj", "qkv_rope_proj", "o_proj",
-                                       "causal_attention", "rmsnorm", "row_sumsq", "qwen_forward", "decode",
-                                       "kv_attention"],
+    ap.add_argument("--only", choices=["forward", "stack", "lm_head", "gate_up_swiglu", "down_proj", "qkv_rope_proj",
+                                       "o_proj", "causal_attention", "rmsnorm", "row_sumsq", "qwen_forward",
+                                       "decode", "kv_attention"],
                     help="profiling helper: time only the graph replay or one kernel kind (268M shapes), "
                          "the Qwen-shaped batched forward (--qwen-batch sequences of 512), cached decoding "
                          "(decode) or the KV-cache attention kernel alone (kv_attention)")
@@ -365,6 +365,63 @@ def _kernel_cases(model, cfg, dev, tokens_per_fwd: int):
     }
 
 
+def _stack_launch(model, tokens):
+    """(closure launching the one-kernel decoder stack on the model's plan for these tokens,
+    closure launching the LM head GEMM on its output, algorithmic HBM bytes per stack launch)."""
+    import torch
+    from tinker_b200.kernels.gemm import linear
+    base = model._model if hasattr(model, "_model") else model
+    plan = base._tinker_stack_plans[tuple(tokens.shape)]
+    emb, layers, norm, head = base._tinker_stack_parts
+    y = plan.hidden_states(tokens)
+    weights = 0
+    for blk in layers:
+        n1, at, n2, ff = (getattr(blk, n) for n in blk._tinker_block_parts)
+        for w in (at.q_proj.weight, at.k_proj.weight, at.v_proj.weight, at.o_proj.weight, ff.gate_proj.weight,
+                  ff.up_proj.weight, ff.down_proj.weight):
+            weights += w.numel() * w.element_size()
+    m, hidden = tokens.numel(), emb.weight.shape[1]
+    # every layer's (folded) weights once, the embedding rows in, the final norm's rows out, its weight
+    nbytes = weights + 2 * m * hidden * 2 + hidden * 2
+    return (lambda: plan.hidden_states(tokens)), (lambda: linear(y, head.weight)), nbytes
+
+
+def _time_launches(fn, steps: int, warmup: int = 3):
+    """Mean ms of ``fn`` launched back to back ``steps`` times (CUDA events on the current stream)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _stack_roofline(model, tokens, peaks, peak_note, steps: int = 200):
+    """Roofline of the forward's dominant kernel, the one-kernel decoder stack: its algorithmic
+    bytes (all layer weights streamed once, embedding rows in, normalised rows out) over its
+    mean launch time, CUDA events around back-to-back launches on the launching stream (each
+    launch streams ~406 MB of weights, more than the 126 MB L2, so no flush is needed)."""
+    stack, head, nbytes = _stack_launch(model, tokens)
+    t_stack = _time_launches(stack, steps) * 1e-3
+    t_head = _time_launches(head, steps) * 1e-3
+    achieved = nbytes / t_stack / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("llama268m-b1s128/stack")
+    return {"kernel": "stack_kernel (embedding + 18 decoder blocks + final RMSNorm, one launch)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic, "bytes_per_launch": nbytes,
+            "us_per_launch": round(t_stack * 1e6, 2), "lm_head_us": round(t_head * 1e6, 2),
+            "note": f"peak {peak_note} (burst copy); launch time from CUDA events over {steps} launches"}
+
+
 def _kernel_rooflines(model, cfg, dev, peaks, peak_note, tokens_per_fwd: int):
     """Time each kernel kind on the model's own weights inside a CUDA graph, cold: graph
     A = [L2 flush, launch] per layer, graph B = [L2 flush] per layer; the kernel's time is
@@ -579,6 +636,21 @@ def run_only(args):
         return
     cfg = LLAMA_268M
     tokens = make_tokens(cfg, 1, 128, seed=1)
+    if args.only in ("stack", "lm_head"):
+        model = tinker_b200.optimize(build_model(cfg, seed=0).to(dev), dtype=torch.float16)
+        tok = tokens.to(dev)
+        with torch.inference_mode():
+            model(tok)  # makes the plan for this shape
+            stack, head, _ = _stack_launch(model, tok)
+            fn = stack if args.only == "stack" else head
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("timed")
+            ms = _time_launches(fn, args.steps, warmup=0)
+            torch.cuda.nvtx.range_pop()
+        print(json.dumps({"only": args.only, "steps": args.steps, "ms_mean": round(ms, 5)}), flush=True)
+        return
     graph = args.only == "forward"
     model = tinker_b200.optimize(build_model(cfg, seed=0).to(dev), dtype=torch.float16, cuda_graph=graph,
                                  graph_input_shape=(1, 128), graph_vocab_size=cfg.vocab_size)
@@ -668,7 +740,9 @@ def run_ours(args):
     clocks = sampler.stop()
 
     # ---- per-kernel rooflines (rank 0 view; every rank runs the same work) ------------------------
-    table, roof = _kernel_rooflines(model, cfg, dev, peaks, peak_note, 128)
+    with torch.inference_mode():
+        roof = _stack_roofline(model, tokens.to(dev), peaks, peak_note)
+    table, _ = _kernel_rooflines(model, cfg, dev, peaks, peak_note, 128)
     weight_bytes = sum(p.numel() * p.element_size() for p in model._model.parameters())
     emb = model._model.embedding.weight
     fwd_bytes = (weight_bytes - emb.numel() * emb.element_size() + 128 * cfg.hidden_size * 2
@@ -738,7 +812,8 @@ def run_ours(args):
                                                   "vs": "reference fp32 eager forward (CPU), same weights/tokens"}}
         if batched_rows is not None:
             qcfg = QWEN25_05B_SHAPED
-            qref = _reference_forward(_reference_cpu_model(qcfg), batched_rows[0])
+            with torch.inference_mode():
+                qref = _reference_forward(_reference_cpu_model(qcfg), batched_rows[0])
             parity["qwen_shaped_b64s512_bf16_graph"] = {
                 **logits_parity(batched_rows[1], qref.float().numpy()),
                 "vs": "reference fp32 eager forward (CPU) of the first and last of the 64 sequences"}
@@ -759,7 +834,7 @@ def run_ours(args):
             "vs_baseline_ref": f"{PUBLISHED_MS} ms, reference README.md:13 (RTX 5080)",
             "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": 128 * 8,
                     "d2h_bytes_per_step": 128 * cfg.vocab_size * 2},
-            "roofline": roof, "roofline_forward": roof_fwd, "kernels": table,
+            "roofline": roof, "roofline_forward": roof_fwd, "kernels_per_block_path": table,
             "gpu_launches": launches_per_fwd * args.steps, "gpu_launches_per_fwd": launches_per_fwd,
             "clocks": clocks, "cpu_baseline": cpu, "parity": parity, "batched": batched, "decode": decode,
         }

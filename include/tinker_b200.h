@@ -52,7 +52,8 @@ TK_API int tk_check_device(int device);
 /* Read (and optionally clear) the sticky device-side error word of the current
  * device. Non-zero means a kernel gave up and its outputs are invalid: 1 = a
  * bounded wait timed out, 2 = a position read from device memory lay beyond a KV
- * cache or RoPE table. Synchronises the device; meant for tests and debugging. */
+ * cache or RoPE table, 3 = a token id read from device memory lay outside the
+ * embedding table. Synchronises the device; meant for tests and debugging. */
 TK_API int tk_device_error(int* code, int clear);
 
 /*
@@ -336,13 +337,61 @@ TK_API int tk_swiglu_ffn(const void* x, int64_t x_row_stride, const void* w_gate
  * reference: it is for callers that cannot allocate - hosts that own all device
  * memory and pass only inputs and outputs, or loops that must not call
  * cudaMalloc/cudaFree. Requires m * f * 2 <= 8 MiB (else TK_ERR_INVALID). The
- * first call on a device looks up the array's address; make it before any
- * stream capture starts. All calls on a device share the array, so calls that
+ * first call in each CUDA context looks up the array's address; make it before
+ * any stream capture starts. All calls on a device share the array, so calls that
  * overlap on the GPU race and must be ordered by the caller.
  */
 TK_API int tk_swiglu_ffn_noalloc(const void* x, int64_t x_row_stride, const void* w_gate, const void* w_up,
                           const void* w_down, void* out, const void* residual, int64_t m, int64_t hidden,
                           int64_t f, int dtype, void* stream);
+
+/*
+ * The whole decoder stack of a short prefill (batch * seq <= 128 rows) in ONE persistent
+ * kernel: token embedding, then per layer the q|k|v projection (attention RMSNorm folded
+ * into wq/wk/wv, RoPE in the epilogue), causal GQA attention, o_proj + residual, gate|up +
+ * SwiGLU (FFN RMSNorm folded into wg/wu), down + residual; then the final RMSNorm. The
+ * arithmetic of the per-block path (tk_linear_rope, tk_causal_attention, tk_linear_ex,
+ * tk_gate_up_swiglu_ex) with kernel boundaries replaced by arrival counters; it replaces the
+ * reference's patched forward of the model's blocks and final norm (benchmarks/bench_e2e.py
+ * :112-138 with tinker/modules/*.py, tinker/kernels/*.py), whose CUDA graph replays one kernel
+ * launch per operation (tinker/optimize.py:153-173). head_dim 64; hidden and intermediate
+ * multiples of 64; weights [out, in] row-major in `dtype`, 16-byte aligned.
+ *
+ * tk_stack_setup (synchronous, not capturable): plans the tiles, encodes the tensor maps of
+ * every weight into `scratch` (tk_stack_scratch_bytes() bytes, 256-byte aligned) and zeroes
+ * its counters. Weights, tables and the embedding must stay at their addresses while the plan
+ * is used. tk_stack_forward (capturable, no host synchronisation): tokens [batch * seq] int64
+ * on the device; y [batch * seq, hidden] receives the final RMSNorm of the last block's output
+ * (the LM head's input). Token ids outside [0, vocab) record device error 3 and read row 0.
+ * Every wait is bounded: a launch whose wait runs out records device error 1, skips the rest
+ * of its work (outputs invalid) and still leaves the scratch ready for the next launch. Calls
+ * sharing one scratch must not overlap on the GPU.
+ */
+typedef struct tk_stack_layer {
+  const void* wq;
+  const void* wk;
+  const void* wv;
+  const void* wo;
+  const void* wg;
+  const void* wu;
+  const void* wd;
+  float eps_attn;
+  float eps_ffn;
+} tk_stack_layer;
+
+TK_API int64_t tk_stack_scratch_bytes(int num_layers, int batch, int seq, int hidden, int num_heads, int num_kv_heads,
+                                      int head_dim, int intermediate);
+TK_API int tk_stack_setup(const tk_stack_layer* layers, int num_layers, int batch, int seq, int hidden, int num_heads,
+                          int num_kv_heads, int head_dim, int intermediate, const void* embedding, int64_t vocab,
+                          const float* cos_table, const float* sin_table, int64_t table_rows, int start_pos,
+                          const void* final_norm_weight, float final_eps, int dtype, void* scratch,
+                          int64_t scratch_bytes);
+TK_API int tk_stack_forward(const int64_t* tokens, void* y, void* scratch, void* stream);
+/* The tile plan of a prepared scratch: out[4 * g .. 4 * g + 3] = (accumulator columns, tiles,
+ * k-splits, k-blocks) of projection g (0 q|k|v, 1 o_proj, 2 gate|up, 3 down); out[16] = CTAs. */
+TK_API int tk_stack_plan(void* scratch, int* out, int n);
+/* Forget the plan tk_stack_setup stored for `scratch` (before freeing it). */
+TK_API int tk_stack_release(void* scratch);
 
 #ifdef __cplusplus
 }

@@ -42,6 +42,12 @@ class StepLayer(ctypes.Structure):
     _fields_ = [("wq", _P), ("wk", _P), ("wv", _P), ("wo", _P), ("wg", _P), ("wu", _P), ("wd", _P),
                 ("k_cache", _P), ("v_cache", _P), ("eps_attn", _F), ("eps_ffn", _F)]
 
+class StackLayer(ctypes.Structure):
+    """``tk_stack_layer`` of tinker_b200.h: one layer of tk_stack_setup's table."""
+    _fields_ = [("wq", _P), ("wk", _P), ("wv", _P), ("wo", _P), ("wg", _P), ("wu", _P), ("wd", _P),
+                ("eps_attn", _F), ("eps_ffn", _F)]
+
+
 # name -> argtypes; every entry point returns int (status)
 SIGNATURES = {
     "tk_version": [],
@@ -72,10 +78,16 @@ SIGNATURES = {
     "tk_decode_step": [_P, _P, _P, _P],
     "tk_decode_step_release": [_P],
     "tk_decode_step_withhold_arrival": [_P, _I],
+    "tk_stack_scratch_bytes": [_I, _I, _I, _I, _I, _I, _I, _I],
+    "tk_stack_setup": [ctypes.POINTER(StackLayer), _I, _I, _I, _I, _I, _I, _I, _I, _P, _I64, _P, _P, _I64, _I, _P,
+                       _F, _I, _P, _I64],
+    "tk_stack_forward": [_P, _P, _P, _P],
+    "tk_stack_plan": [_P, ctypes.POINTER(_I), _I],
+    "tk_stack_release": [_P],
 }
 
 # entry points whose return value is not a status
-RESTYPES = {"tk_kv_attention_workspace": _I64, "tk_decode_step_scratch_bytes": _I64}
+RESTYPES = {"tk_kv_attention_workspace": _I64, "tk_decode_step_scratch_bytes": _I64, "tk_stack_scratch_bytes": _I64}
 
 _lock = threading.Lock()
 _lib = None
@@ -152,7 +164,7 @@ def stream_ptr(device: torch.device) -> int:
 
 def device_error(clear: bool = True) -> int:
     """Sticky device-side error word (0: none; 1: a bounded wait timed out; 2: a device-side
-    position beyond a KV cache or RoPE table)."""
+    position beyond a KV cache or RoPE table; 3: a token id outside the embedding table)."""
     code = _I(0)
     check(lib().tk_device_error(ctypes.byref(code), 1 if clear else 0), "tk_device_error")
     return code.value

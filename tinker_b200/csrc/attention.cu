@@ -1,28 +1,29 @@
 // Fused RoPE + GQA/MQA/MHA causal attention on tcgen05 tensor cores.
 //
-// One CTA computes a 128-row query tile of one (batch, query head) with four
-// warp roles working through mbarriers:
-//   * warp 4 (TMA): loads the raw Q tile once and streams the raw K and V tiles
-//     of KV head h / groups through a two-stage ring straight from the
-//     [batch, seq, heads, head_dim] projection layout (token strides are free, so
-//     q/k/v may be column slices of one fused QKV output) into 128-byte-swizzled
-//     shared memory.
-//   * warps 6-7 (RoPE): rotate the interleaved pairs of every K row in place in
-//     shared memory, in fp32, rounding back to the input dtype as the reference
-//     does before its attention kernel (tinker/kernels/fused_attention.py:203-214,
-//     :53-69). Warps 0-3 rotate the Q tile the same way, once.
-//   * warp 5 (MMA): S_j = Q K_j^T as tcgen05.mma (M=128, N=128, K=head_dim) into
-//     one of two TMEM S buffers, so S_{j+1} is computed while S_j is in softmax;
-//     then O += P_j V_j with V as an MN-major operand into the TMEM O accumulator.
-//   * warps 0-3 (softmax, thread i owns query row i): read S_j with tcgen05.ld,
-//     mask the diagonal tile, run the online softmax with exp2, write P_j (rounded
-//     to the input dtype) to shared memory and rescale the running O in TMEM.
-//     The running maximum is only moved when a tile raises it by more than
-//     2^8 (a lazy rescale): P stays below 256 and O is rescaled on few tiles.
-//     The final O / l is written by the same threads.
-// Causal tiles above the diagonal are skipped. The arithmetic follows
-// _attention_kernel (tinker/kernels/fused_attention.py:74-154): scale
-// 1/sqrt(head_dim), running max / sum in fp32, output divided by the sum.
+// One CTA computes a PAIR of 128-row query tiles (a = 2 * blk, b = 2 * blk + 1) of one
+// (batch, query head); the heaviest pairs are scheduled first. 384 threads, five roles
+// working through mbarriers:
+//   * warp 8 (TMA): loads the two raw Q tiles once, then streams K_0, V_0, K_1, V_1, ...
+//     of KV head h / groups through a ring of 4 (head_dim 64) or 3 (head_dim 128) slots,
+//     straight from the [batch, seq, heads, head_dim] projection layout (token strides
+//     are free, so q/k/v may be column slices of one fused q|k|v output) into
+//     128-byte-swizzled shared memory. Tile b needs one key tile more than tile a.
+//   * warps 10-11 (RoPE, drop-in entry only): rotate the interleaved pairs of every K row
+//     in place in shared memory, in fp32, rounding back to the input dtype as the
+//     reference does before its attention kernel (tinker/kernels/fused_attention.py
+//     :203-214, :53-69). The softmax warps rotate their Q tile the same way, once.
+//   * warp 9 (MMA, one thread): S_a = Q_a K_j^T and S_b = Q_b K_j^T as tcgen05.mma
+//     (M=128, N=128, K=head_dim) into two TMEM S buffers, then O_a += P_a V_j and
+//     O_b += P_b V_j with V as an MN-major operand into two TMEM O accumulators.
+//   * warps 0-3 (tile a) and 4-7 (tile b), softmax, thread i owns query row i: read S
+//     with tcgen05.ld, mask the diagonal tile, run the online softmax with exp2, write P
+//     (rounded to the input dtype) to shared memory and rescale the running O in TMEM.
+//     The running maximum is only moved when a tile raises it by more than 2^8 (a lazy
+//     rescale): P stays below 256 and O is rescaled on few tiles. The final O / l is
+//     written by the same threads.
+// Causal tiles above the diagonal are skipped. The arithmetic follows _attention_kernel
+// (tinker/kernels/fused_attention.py:74-154): scale 1/sqrt(head_dim), running max / sum
+// in fp32, output divided by the sum.
 #include <algorithm>
 #include <cmath>
 

@@ -21,6 +21,7 @@
 
 #define TK_DEVERR_TIMEOUT 1
 #define TK_DEVERR_POSITION 2  // a position read from device memory is beyond a cache or table
+#define TK_DEVERR_TOKEN 3     // a token id read from device memory is outside the embedding table
 
 // Sticky device-side error word (first error code wins); read by tk_device_error().
 extern __device__ int g_tk_device_error;

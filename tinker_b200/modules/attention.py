@@ -17,6 +17,7 @@ import torch.nn as nn
 from tinker_b200.kernels.fused_attention import causal_attention, fused_attention, precompute_rope_tables
 from tinker_b200.kernels.gemm import linear, linear_rope
 from tinker_b200.kernels.kv_cache import kv_append, kv_attention
+from tinker_b200 import torch_ops
 from tinker_b200.modules._roles import attention_projections
 
 # Query rows per kv head (groups * new tokens) above which a prompt at position 0 runs on the
@@ -85,27 +86,11 @@ class TinKerAttention(nn.Module):
             a = self.cached_attention(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, kv_cache,
                                       start_pos, position)
             return linear(a, self.o_proj.weight, residual=residual)
-        hq = self.num_heads * self.head_dim
-        hkv = self.num_kv_heads * self.head_dim
-        if (x.dim() == 3 and self.cos_table.dtype == torch.float32 and self.sin_table.dtype == torch.float32
-                and self.head_dim % 32 == 0 and hq % self.head_dim == 0):
-            # RoPE in the projection epilogue, attention on the rotated q/k
-            qkv = linear_rope(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
-                              self.cos_table, self.sin_table, self.head_dim, start_pos)
-            attn_out = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:],
-                                        self.num_heads, self.num_kv_heads, self.head_dim)
-            return linear(attn_out, self.o_proj.weight, residual=residual)
-        qkv = linear(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
-        q = qkv[..., :hq]
-        k = qkv[..., hq:hq + hkv]
-        v = qkv[..., hq + hkv:]
-        attn_out = fused_attention(
-            q, k, v,
-            self.cos_table, self.sin_table,
-            self.num_heads, self.num_kv_heads, self.head_dim,
-            start_pos=start_pos,
-        )
-        return linear(attn_out, self.o_proj.weight, residual=residual)
+        args = (x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.o_proj.weight, self.cos_table,
+                self.sin_table, self.num_heads, self.num_kv_heads, self.head_dim, int(start_pos), residual)
+        if torch_ops.compiling():  # one opaque node for torch.compile (tinker_b200.torch_ops)
+            return torch.ops.tinker.attention(*args)
+        return attention_forward(*args)
 
     def cached_attention(self, x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, kv_cache,
                          start_pos: int = 0, position: torch.Tensor | None = None,
@@ -162,6 +147,25 @@ class TinKerAttention(nn.Module):
     def extra_repr(self) -> str:
         return (f"hidden_size={self.hidden_size}, heads={self.num_heads}/{self.num_kv_heads} (q/kv), "
                 f"head_dim={self.head_dim}, rope_theta={self.rope_theta}")
+
+
+def attention_forward(x, wq, wk, wv, wo, cos_table, sin_table, num_heads: int, num_kv_heads: int, head_dim: int,
+                      start_pos: int = 0, residual=None):
+    """``TinKerAttention.forward`` without a KV cache: q|k|v projection, RoPE, causal GQA
+    attention, o_proj (+ ``residual`` in its epilogue)."""
+    hq = num_heads * head_dim
+    hkv = num_kv_heads * head_dim
+    if (x.dim() == 3 and cos_table.dtype == torch.float32 and sin_table.dtype == torch.float32
+            and head_dim % 32 == 0 and hq % head_dim == 0):
+        # RoPE in the projection epilogue, attention on the rotated q/k
+        qkv = linear_rope(x, wq, wk, wv, cos_table, sin_table, head_dim, start_pos)
+        attn_out = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], num_heads,
+                                    num_kv_heads, head_dim)
+        return linear(attn_out, wo, residual=residual)
+    qkv = linear(x, wq, wk, wv)
+    attn_out = fused_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], cos_table, sin_table,
+                               num_heads, num_kv_heads, head_dim, start_pos=start_pos)
+    return linear(attn_out, wo, residual=residual)
 
 
 def _head_layout(source: nn.Module, hidden: int, q_rows: int, kv_rows: int) -> tuple[int, int, int]:

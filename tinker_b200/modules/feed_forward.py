@@ -9,6 +9,7 @@ applied in the epilogue, then the down projection. The ``gate_proj`` /
 import torch
 import torch.nn as nn
 
+from tinker_b200 import torch_ops
 from tinker_b200.kernels.gemm import swiglu_ffn
 from tinker_b200.modules._roles import swiglu_weights
 
@@ -31,7 +32,10 @@ class TinKerSwiGLU(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """``down(silu(gate(x)) * up(x))``; with ``residual`` the sum is added in the epilogue."""
-        return swiglu_ffn(x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight, residual)
+        args = (x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight, residual)
+        if torch_ops.compiling():  # one opaque node for torch.compile (tinker_b200.torch_ops)
+            return torch.ops.tinker.swiglu_ffn(*args)
+        return swiglu_ffn(*args)
 
     @classmethod
     def from_module(cls, source: nn.Module) -> "TinKerSwiGLU":

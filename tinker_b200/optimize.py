@@ -7,8 +7,11 @@
   2. half precision (``dtype``), then decoder-block fusion (``fuse_blocks``)
   3. int8 dynamic quantization: not part of the B200 path (the reference's is a
      CPU-only ``quantize_dynamic``); reported and skipped
-  4. ``compile``: accepted and not used - the patched forward already runs
-     hand-written kernels, and the CUDA graph removes the launch overhead
+  4. ``compile=True``: ``torch.compile(model, mode=compile_mode)``; the patched modules
+     call registered torch ops while being compiled (``tinker_b200.torch_ops``), so the
+     kernels are single graph nodes, and block fusion / the one-kernel stack (Python-level
+     rewrites that do not trace) are skipped. The default (None) does not compile: the
+     hand-written kernels and the CUDA graph already remove what compiling would
   5. CUDA backend flags (TF32, cuDNN benchmark, flash SDPA) as in the reference
   6. optional CUDA graph capture of the whole forward (static shapes)
 """
@@ -24,6 +27,7 @@ from tinker_b200 import _lib
 from tinker_b200.fusion import fuse_decoder_blocks, share_rope_tables
 from tinker_b200.kernels._common import stable_weights
 from tinker_b200.patch import patch_model
+from tinker_b200.stack import install_stack_forward
 
 
 def optimize(
@@ -44,6 +48,7 @@ def optimize(
     graph_clone_output: bool = True,
     fuse_blocks: bool = True,
     fold_norms: bool = True,
+    stack_kernel: bool = False,
 ) -> nn.Module:
     """optimize a model for inference on a B200.
 
@@ -53,7 +58,10 @@ def optimize(
     itself; ``fuse_blocks`` (default True) gives qualifying pre-norm decoder blocks
     a forward whose residual adds run inside the GEMM epilogues
     (``tinker_b200.fusion``), after checking the block's dataflow; ``fold_norms``
-    (default True) also folds those blocks' RMSNorms into the GEMMs after them.
+    (default True) also folds those blocks' RMSNorms into the GEMMs after them;
+    ``stack_kernel`` (default True) runs a forward over at most 128 token rows of a
+    decoder LM whose blocks were fused and folded as one persistent kernel for the
+    embedding, all blocks and the final norm (``tinker_b200.stack``), then the LM head.
     """
     model.eval()
     params = list(model.parameters())
@@ -82,16 +90,29 @@ def optimize(
     if replace_attention:
         share_rope_tables(model)
 
-    if fuse_blocks and replace_attention and replace_ffn and replace_norm:
+    if compile and fuse_blocks and verbose:
+        print("  [tinker] compile=True: decoder blocks left unfused (their Python-level fusion does not trace)")
+    if fuse_blocks and not compile and replace_attention and replace_ffn and replace_norm:
         n = fuse_decoder_blocks(model, verbose=verbose, fold_norms=fold_norms)
         if verbose:
             print(f"  [tinker] fused {n} decoder blocks (residual adds in the GEMM epilogues)")
+        if stack_kernel and fold_norms and n:
+            install_stack_forward(model, verbose=verbose)
 
     if quantize and verbose:
         print("  [tinker] int8 quantization skipped: not part of the B200 kernel path")
 
-    if compile and verbose:
-        print(f"  [tinker] torch.compile (mode={compile_mode}) not used: the forward runs sm_100a kernels")
+    if compile:
+        # the TinKer* modules call registered ops while compiled (tinker_b200.torch_ops), so the
+        # patched model traces without graph breaks; a failure keeps the eager model, as in the
+        # reference (tinker/optimize.py:77-88)
+        if verbose:
+            print(f"  [tinker] torch.compile (mode={compile_mode})")
+        try:
+            model = torch.compile(model, mode=compile_mode)
+        except Exception as e:
+            if verbose:
+                print(f"  [tinker] compile failed: {e}")
 
     torch.backends.cudnn.benchmark = True
     torch.backends.cuda.matmul.allow_tf32 = True
