@@ -66,7 +66,7 @@ def test_stack_268m_against_oracle_and_launches():
     tokens = make_tokens(cfg, 1, 128, seed=1)
     cpu_model = build_model(cfg, seed=0)
     ref = _oracle_logits(cpu_model, tokens, cfg).astype(np.float64)
-    model = tinker_b200.optimize(cpu_model.to("cuda"), dtype=torch.float16)
+    model = tinker_b200.optimize(cpu_model.to("cuda"), dtype=torch.float16, stack_kernel=True)
     with torch.inference_mode():
         out = np32(model(tokens.cuda()))
         n0 = _lib.launch_counter[0]
@@ -137,7 +137,7 @@ def test_stack_in_cuda_graph_and_larger_inputs_fall_back():
     cfg = TINY.with_(num_layers=2)
     tokens = make_tokens(cfg, 2, 64, seed=8).cuda()
     g = tinker_b200.optimize(build_model(cfg, seed=9).cuda(), dtype=torch.float16, cuda_graph=True,
-                             graph_input_shape=(2, 64), graph_vocab_size=cfg.vocab_size)
+                             graph_input_shape=(2, 64), graph_vocab_size=cfg.vocab_size, stack_kernel=True)
     ref = tinker_b200.optimize(build_model(cfg, seed=9).cuda(), dtype=torch.float16, stack_kernel=False)
     assert type(g).__name__ == "_CUDAGraphWrapper" and (2, 64) in g._model._tinker_stack_plans
     big = make_tokens(cfg, 3, 50, seed=9).cuda()
