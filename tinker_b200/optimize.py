@@ -59,7 +59,7 @@ def optimize(
     a forward whose residual adds run inside the GEMM epilogues
     (``tinker_b200.fusion``), after checking the block's dataflow; ``fold_norms``
     (default True) also folds those blocks' RMSNorms into the GEMMs after them;
-    ``stack_kernel`` (default True) runs a forward over at most 128 token rows of a
+    ``stack_kernel`` (default False) runs a forward over at most 128 token rows of a
     decoder LM whose blocks were fused and folded as one persistent kernel for the
     embedding, all blocks and the final norm (``tinker_b200.stack``), then the LM head.
     """
