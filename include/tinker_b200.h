@@ -390,6 +390,13 @@ TK_API int tk_stack_forward(const int64_t* tokens, void* y, void* scratch, void*
 /* The tile plan of a prepared scratch: out[4 * g .. 4 * g + 3] = (accumulator columns, tiles,
  * k-splits, k-blocks) of projection g (0 q|k|v, 1 o_proj, 2 gate|up, 3 down); out[16] = CTAs. */
 TK_API int tk_stack_plan(void* scratch, int* out, int n);
+/* Diagnostics (no reference counterpart): with `trace` non-NULL, later tk_stack_forward launches
+ * on `scratch` write %globaltimer stamps (ns) of 8 events per CTA and schedule stage to
+ * trace[(cta * (2 + 5 * num_layers) + stage) * 8 + event] (events: producer saw the stage's
+ * dependency, producer issued its first weight tiles, MMA committed, epilogue saw its first
+ * accumulator, its first tile's k-splits, the stage's dependency, arrived; attention S ready).
+ * NULL turns it off (the default). */
+TK_API int tk_stack_trace(void* scratch, unsigned long long* trace);
 /* Forget the plan tk_stack_setup stored for `scratch` (before freeing it). */
 TK_API int tk_stack_release(void* scratch);
 

@@ -84,6 +84,7 @@ SIGNATURES = {
     "tk_stack_forward": [_P, _P, _P, _P],
     "tk_stack_plan": [_P, ctypes.POINTER(_I), _I],
     "tk_stack_release": [_P],
+    "tk_stack_trace": [_P, _P],
 }
 
 # entry points whose return value is not a status

@@ -88,6 +88,11 @@ constexpr int SMEM_BYTES = 1024 + RSTD_OFF + BM * 4;
 constexpr uint32_t T_ACC = 0, T_S = 128, T_O = 256, TMEM_COLS = 512;
 
 enum GemmKind { G_QKV = 0, G_O = 1, G_GU = 2, G_D = 3 };
+// trace events (tk_stack_trace): producer saw the stage's dependency / issued its first weight
+// tiles; MMA committed the stage's last item; epilogue saw its first accumulator / its first
+// tile's k-splits / the stage's dependency, arrived on the stage; attention S ready
+enum TraceEvent { EV_DEP = 0, EV_W = 1, EV_MMA = 2, EV_ACC = 3, EV_TILE = 4, EV_EDEP = 5, EV_ARRIVE = 6, EV_S = 7,
+                  EV_PW = 8, EV_RED = 9, EV_O = 10, TRACE_EVENTS = 12 };
 enum : int { K_QKV = 0, K_ATT = 1, K_O = 2, K_GU = 3, K_D = 4, STAGES_PER_LAYER = 5 };
 
 struct Gemm {
@@ -126,6 +131,9 @@ struct Params {
   const void* final_w;
   float final_eps;
   float scale_log2;  // log2(e) / sqrt(head_dim)
+  // diagnostics (null: off): %globaltimer of event e of stage s in CTA c at
+  // trace[(c * exit_counter(num_layers) + s) * TRACE_EVENTS + e]
+  unsigned long long* trace;
 };
 
 __host__ __device__ inline int stage_of(int layer, int kind) { return 1 + STAGES_PER_LAYER * layer + kind; }
@@ -136,6 +144,12 @@ __host__ __device__ inline int abort_word(int layers) { return exit_counter(laye
 __host__ __device__ inline int tile_counter(const Params& p, int layer, int gk, int tile) {
   return abort_word(p.num_layers) + 1 + (layer * 4 + gk) * p.max_tiles + tile;
 }
+
+#define TK_TRACE(s, e)                                                                               \
+  do {                                                                                               \
+    if (p.trace) p.trace[(static_cast<size_t>(blockIdx.x) * exit_counter(p.num_layers) + (s)) * TRACE_EVENTS + (e)] = \
+        globaltimer();                                                                               \
+  } while (0)
 
 // ---- cross-CTA synchronisation ------------------------------------------------------------
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -155,14 +169,27 @@ __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence
 // named barrier of the four epilogue warps
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // Wait until *c >= target (acquire). False when the wait runs out (device error 1 recorded,
-// the launch's abort word set) or another wait of this launch already ran out.
+// the launch's abort word set) or another wait of this launch already ran out. Polls with
+// relaxed loads and a short back-off (up to 296 pollers share a counter) and fences once.
 __device__ bool wait_count(const unsigned* c, unsigned target, unsigned* abort) {
   if (ld_acquire_u32(c) >= target) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    for (int i = 0; i < 16; ++i)
-      if (ld_acquire_u32(c) >= target) return true;
+    for (int i = 0; i < 16; ++i) {
+      if (ld_relaxed_u32(c) >= target) {
+        fence_acquire_gpu();
+        return true;
+      }
+      __nanosleep(32);
+    }
     if (aborted(abort)) return false;
     if (globaltimer() - t0 > TK_WAIT_LIMIT_NS) {
       give_up(abort);
@@ -214,11 +241,66 @@ __device__ __forceinline__ float store8(void* base, int64_t idx, const float (&v
   *reinterpret_cast<uint4*>(static_cast<typename D::T*>(base) + idx) = make_uint4(w[0], w[1], w[2], w[3]);
   return sq;
 }
-__device__ __forceinline__ void add_partial8(const float* src, float (&v)[8]) {
-  const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
-  const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+// v[0..8) += sum over k-splits sp = 0..split-1 of the 8 floats at src + sp * stride, in split
+// order (deterministic); the loads of six splits are issued before any of them is added, so a
+// deep split costs ceil(split / 6) L2 round trips, not one per split.
+__device__ __forceinline__ void add8(float (&v)[8], const float4& a, const float4& b) {
   v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
   v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+}
+__device__ __forceinline__ void sum_partials8(const float* src, int64_t stride, int split, float (&v)[8]) {
+  for (int s0 = 0; s0 < split; s0 += 6) {
+    float4 a[6], b[6];
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      if (s0 + j < split) {
+        const float4* q = reinterpret_cast<const float4*>(src + (s0 + j) * stride);
+        a[j] = __ldcg(q);
+        b[j] = __ldcg(q + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 6; ++j)
+      if (s0 + j < split) add8(v, a[j], b[j]);
+  }
+}
+// The same for the gate and the up halves of a gate|up tile at once (four splits per round).
+__device__ __forceinline__ void sum_partials8x2(const float* src_g, const float* src_u, int64_t stride, int split,
+                                                float (&g)[8], float (&u)[8]) {
+  for (int s0 = 0; s0 < split; s0 += 4) {
+    float4 a[4], b[4], c[4], d[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (s0 + j < split) {
+        const float4* q = reinterpret_cast<const float4*>(src_g + (s0 + j) * stride);
+        const float4* w = reinterpret_cast<const float4*>(src_u + (s0 + j) * stride);
+        a[j] = __ldcg(q);
+        b[j] = __ldcg(q + 1);
+        c[j] = __ldcg(w);
+        d[j] = __ldcg(w + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (s0 + j < split) {
+        add8(g, a[j], b[j]);
+        add8(u, c[j], d[j]);
+      }
+    }
+  }
+}
+// Sum of the `parts` 32-column sums of squares of row `row` ([parts, BM] layout), in part order,
+// with eight loads in flight.
+__device__ __forceinline__ float row_ssq(const float* ssq, int parts, int row) {
+  float t = 0.f;
+  for (int i0 = 0; i0 < parts; i0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = i0 + j < parts ? __ldcg(ssq + (i0 + j) * BM + row) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += v[j];
+  }
+  return t;
 }
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
@@ -282,6 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
                 ok = wait_count(p.counters + s - 1, grid, abort);
                 fence_proxy_async_global();
                 dep = true;
+                TK_TRACE(s, EV_DEP);
               }
               if (ok) {
                 const int b = it / p.heads, hd = it % p.heads, kvh = hd / (p.heads / p.kv_heads);
@@ -308,6 +391,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
             const int kb0 = r * G.num_kb / G.split, kb1 = (r + 1) * G.num_kb / G.split;
             // weights first: they do not depend on the previous stage
             ok = ok && (n_gemm == 0 || wait_bar(bars + B_W_FREE, (n_gemm - 1) & 1, abort));
+            if (it == static_cast<int>(blockIdx.x)) TK_TRACE(s, EV_W);
             if (ok) {
               mbar_arrive_expect_tx(bars + B_W_FULL, (kb1 - kb0) * G.bn * BK * 2);
               ++w_arms;
@@ -332,6 +416,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
               ok = wait_count(p.counters + s - 1, grid, abort);
               fence_proxy_async_global();
               dep = true;
+              TK_TRACE(s, EV_DEP);
             }
             if (ok) {
               for (int kb = kb0; kb < kb1; ++kb) {
@@ -392,6 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
                 umma_commit(bars + B_O_FULL);
                 umma_commit(bars + B_A_FREE);
               }
+              TK_TRACE(stage_of(l, kind), EV_MMA);
               ++n_att;
             }
             continue;
@@ -421,6 +507,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
               umma_commit(bars + B_W_FREE);
               umma_commit(bars + B_A_FREE);
             }
+            TK_TRACE(stage_of(l, kind), EV_MMA);
             ++n_gemm;
           }
         }
@@ -441,11 +528,17 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
     auto arrive = [&](int s) {
       __threadfence();
       epi_sync();
-      if (et == 0) red_release_add(p.counters + s, 1);
+      if (et == 0) {
+        red_release_add(p.counters + s, 1);
+        TK_TRACE(s, EV_ARRIVE);
+      }
     };
     // all 128 threads: wait for stage s to be complete (thread 0 polls), ok made uniform
     auto depend = [&](int s) {
-      if (et == 0) flag_s[0] = (ok && wait_count(p.counters + s, grid, abort)) ? 1 : 0;
+      if (et == 0) {
+        flag_s[0] = (ok && wait_count(p.counters + s, grid, abort)) ? 1 : 0;
+        TK_TRACE(s + 1, EV_EDEP);
+      }
       epi_sync();
       ok = ok && flag_s[0] != 0;
       epi_sync();
@@ -482,44 +575,54 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
             const int i = trow;  // query row within the sequence's tile
             ok = ok && wait_bar(bars + B_S_FULL, n_att & 1, abort);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+            if (et == 0) TK_TRACE(s, EV_S);
             float l_sum = 1.f;
             if (ok) {
               tc_fence_after();
-              float sv[BM];
-              tmem_load128(tmem + T_S + lane_off, sv);
-              // causal within the sequence: key j visible iff j <= i and j < seq
+              // causal within the sequence: key j visible iff j <= i and j < seq. S is read from
+              // TMEM in two 64-key halves, twice (maximum, then exponentials), to bound registers.
+              const int jmax = min(i, p.seq - 1);
               float mx = -INFINITY;
+#pragma unroll 1
+              for (int hh = 0; hh < 2; ++hh) {
+                float sv[64];
+                tmem_load64(tmem + T_S + lane_off + hh * 64, sv);
 #pragma unroll
-              for (int j = 0; j < BM; ++j) {
-                if (j > i || j >= p.seq) sv[j] = -INFINITY;
-                mx = fmaxf(mx, sv[j]);
+                for (int j = 0; j < 64; ++j)
+                  if (hh * 64 + j <= jmax) mx = fmaxf(mx, sv[j]);
               }
               const float neg_m = -mx * p.scale_log2;
               float acc = 0.f;
+              uint8_t* prow = a_reg + ATT_P;
+#pragma unroll 1
+              for (int hh = 0; hh < 2; ++hh) {
+                float sv[64];
+                tmem_load64(tmem + T_S + lane_off + hh * 64, sv);
 #pragma unroll
-              for (int j = 0; j < BM; ++j) {
-                sv[j] = exp2_approx(fmaf(sv[j], p.scale_log2, neg_m));
-                acc += sv[j];
+                for (int j = 0; j < 64; ++j) {
+                  sv[j] = hh * 64 + j <= jmax ? exp2_approx(fmaf(sv[j], p.scale_log2, neg_m)) : 0.f;
+                  acc += sv[j];
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * q], sv[c * 8 + 2 * q + 1]);
+                    w[q] = *reinterpret_cast<uint32_t*>(&hv);
+                  }
+                  uint8_t* dst = prow + hh * (BM * 128) + i * 128 + (((c & 7) ^ (i & 7)) * 16);
+                  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
               }
               l_sum = acc;
-              uint8_t* prow = a_reg + ATT_P;
-#pragma unroll
-              for (int c = 0; c < BM / 8; ++c) {
-                uint32_t w[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * q], sv[c * 8 + 2 * q + 1]);
-                  w[q] = *reinterpret_cast<uint32_t*>(&hv);
-                }
-                uint8_t* dst = prow + (c >> 3) * (BM * 128) + i * 128 + (((c & 7) ^ (i & 7)) * 16);
-                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-              }
               fence_proxy_async_smem();
             }
             tc_fence_before();
             mbar_arrive(bars + B_P_FULL);
             ok = ok && wait_bar(bars + B_O_FULL, n_att & 1, abort);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+            if (et == 0) TK_TRACE(s, EV_O);
             if (ok) {
               tc_fence_after();
               const float inv_l = 1.0f / l_sum;
@@ -555,8 +658,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
           if (gk == G_QKV || gk == G_GU) {  // 1/rms of the input rows of the folded RMSNorm
             const float* ssq = gk == G_QKV ? p.ssq_x : p.ssq_h;
             const float eps = p.eps[2 * l + (gk == G_GU ? 1 : 0)];
-            float t = 0.f;
-            for (int i = 0; i < parts; ++i) t += __ldcg(ssq + i * BM + et);
+            const float t = row_ssq(ssq, parts, et);
             rstd_s[et] = rsqrtf(t * (1.0f / static_cast<float>(H)) + eps);
             epi_sync();
           }
@@ -569,6 +671,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
           // 1. this k-split's accumulator rows to the partial buffer
           ok = ok && wait_bar(bars + B_MMA_DONE, n_gemm & 1, abort);
           ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+          if (et == 0 && it == static_cast<int>(blockIdx.x)) TK_TRACE(s, EV_ACC);
           if (ok) {
             tc_fence_after();
             float4* dst = reinterpret_cast<float4*>(part + static_cast<int64_t>(trow) * G.bn);
@@ -585,6 +688,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
           // 2. wait for the tile's other k-splits
           __threadfence();
           epi_sync();
+          if (et == 0 && it == static_cast<int>(blockIdx.x)) TK_TRACE(s, EV_PW);
           if (et == 0) {
             int good = ok ? 1 : 0;
             if (good) {
@@ -592,32 +696,34 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
               red_release_add(cnt, 1);
               good = wait_count(cnt, G.split, abort) ? 1 : 0;
               __threadfence();
+              if (it == static_cast<int>(blockIdx.x)) TK_TRACE(s, EV_TILE);
             }
             flag_s[0] = good;
           }
           epi_sync();
           ok = ok && flag_s[0] != 0;
           epi_sync();
-          // 3. reduce the 16-row groups this k-split owns, then the epilogue
-          int groups[8], ng = 0;
-          for (int g = r; g < 8; g += G.split) groups[ng++] = g;
-          const int units = ng * 16 * cpr;
+          // 3. reduce this k-split's share of the tile's (row, 8-column chunk) units - the m * cpr
+          // units in even shares whose bounds are multiples of 4, so the four units of a 32-column
+          // chunk stay together - then the epilogue. All loads a unit needs (every k-split's
+          // partial, the residual, the RoPE angles) go out before any result is used.
+          const int total = p.m * cpr;
+          const int align = cpr % 4 == 0 ? 4 : 1;  // 4 for the stages that write row statistics
+          auto bound = [&](int q) { return q >= G.split ? total : min(total, (q * total / G.split + align - 1) / align * align); };
+          const int u0 = bound(r), u1 = bound(r + 1);
           const float* tile_part = p.partial + static_cast<int64_t>(tile * G.split) * BM * G.bn;
-          for (int base = 0; base < units; base += EPI_THREADS) {
+          const int64_t pstride = static_cast<int64_t>(BM) * G.bn;
+          for (int base = u0; base < u1; base += EPI_THREADS) {
             const int u = base + et;
-            const bool valid = ok && u < units;
-            const int rr = valid ? u / cpr : 0, ch = valid ? u % cpr : 0;
-            const int row = groups[rr >> 4] * 16 + (rr & 15);
+            const bool valid = ok && u < u1;
+            const int row = valid ? u / cpr : 0, ch = valid ? u % cpr : 0;
             float sq = 0.f;
             int col = 0;
-            if (valid && row < p.m) {
+            if (valid) {
               if (gk == G_GU) {
                 float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, uv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                for (int sp = 0; sp < G.split; ++sp) {
-                  const float* src = tile_part + (static_cast<int64_t>(sp) * BM + row) * G.bn + ch * 8;
-                  add_partial8(src, gv);
-                  add_partial8(src + G.bn / 2, uv);
-                }
+                const float* src = tile_part + static_cast<int64_t>(row) * G.bn + ch * 8;
+                sum_partials8x2(src, src + G.bn / 2, pstride, G.split, gv, uv);
                 col = tile * (G.bn / 2) + ch * 8;
                 if (col < G.n) {
                   const float rs = rstd_s[row];
@@ -626,51 +732,55 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
                   for (int e = 0; e < 8; ++e) v[e] = silu_mul(gv[e] * rs, uv[e] * rs);
                   store8<DT>(p.act, static_cast<int64_t>(row) * p.inter + col, v);
                 }
-              } else {
-                float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                for (int sp = 0; sp < G.split; ++sp)
-                  add_partial8(tile_part + (static_cast<int64_t>(sp) * BM + row) * G.bn + ch * 8, v);
+              } else if (gk == G_QKV) {
                 col = tile * G.bn + ch * 8;
-                if (gk == G_QKV) {
-                  const float rs = rstd_s[row];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) v[e] *= rs;
-                  if (col < p.q_w + p.kv_w) {
-                    // the projection's value rounded to the model dtype, then the interleaved
-                    // pair rotation in fp32 at the row's position (rounded again when stored)
-                    const int64_t pos = static_cast<int64_t>(p.start_pos) + row % p.seq;
-                    const int i0 = (col % HEAD_DIM) >> 1;
-                    const float4 c4 = *reinterpret_cast<const float4*>(p.cos_t + pos * (HEAD_DIM / 2) + i0);
-                    const float4 s4 = *reinterpret_cast<const float4*>(p.sin_t + pos * (HEAD_DIM / 2) + i0);
-                    const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                      const float x0 = Dx::to_f(Dx::from_f(v[2 * e])), x1 = Dx::to_f(Dx::from_f(v[2 * e + 1]));
-                      v[2 * e] = x0 * cs[e] - x1 * sn[e];
-                      v[2 * e + 1] = x0 * sn[e] + x1 * cs[e];
-                    }
-                  }
-                  store8<DT>(p.qkv, static_cast<int64_t>(row) * (p.q_w + 2 * p.kv_w) + col, v);
-                } else {
-                  // o_proj adds x and writes h; down_proj adds h and writes the block output x
-                  const void* res = gk == G_O ? p.x : p.h;
-                  void* out = gk == G_O ? p.h : p.x;
-                  float rv[8];
-                  load8<DT>(res, static_cast<int64_t>(row) * H + col, rv);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) v[e] += rv[e];
-                  sq = store8<DT>(out, static_cast<int64_t>(row) * H + col, v);
+                const bool rope = col < p.q_w + p.kv_w;
+                const int64_t pos = static_cast<int64_t>(p.start_pos) + row % p.seq;
+                const int i0 = (col % HEAD_DIM) >> 1;
+                float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (rope) {
+                  c4 = __ldg(reinterpret_cast<const float4*>(p.cos_t + pos * (HEAD_DIM / 2) + i0));
+                  s4 = __ldg(reinterpret_cast<const float4*>(p.sin_t + pos * (HEAD_DIM / 2) + i0));
                 }
+                float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                sum_partials8(tile_part + static_cast<int64_t>(row) * G.bn + ch * 8, pstride, G.split, v);
+                const float rs = rstd_s[row];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] *= rs;
+                if (rope) {
+                  // the projection's value rounded to the model dtype, then the interleaved pair
+                  // rotation in fp32 at the row's position (rounded again when stored)
+                  const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float x0 = Dx::to_f(Dx::from_f(v[2 * e])), x1 = Dx::to_f(Dx::from_f(v[2 * e + 1]));
+                    v[2 * e] = x0 * cs[e] - x1 * sn[e];
+                    v[2 * e + 1] = x0 * sn[e] + x1 * cs[e];
+                  }
+                }
+                store8<DT>(p.qkv, static_cast<int64_t>(row) * (p.q_w + 2 * p.kv_w) + col, v);
+              } else {
+                // o_proj adds x and writes h; down_proj adds h and writes the block output x
+                col = tile * G.bn + ch * 8;
+                const void* res = gk == G_O ? p.x : p.h;
+                void* out = gk == G_O ? p.h : p.x;
+                float rv[8];
+                load8<DT>(res, static_cast<int64_t>(row) * H + col, rv);
+                float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                sum_partials8(tile_part + static_cast<int64_t>(row) * G.bn + ch * 8, pstride, G.split, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] += rv[e];
+                sq = store8<DT>(out, static_cast<int64_t>(row) * H + col, v);
               }
             }
             if (gk == G_O || gk == G_D) {
               // row statistics for the next folded RMSNorm: the four lanes of a 32-column chunk
               sq += __shfl_xor_sync(0xffffffffu, sq, 1);
               sq += __shfl_xor_sync(0xffffffffu, sq, 2);
-              if (valid && row < p.m && (et & 3) == 0)
-                (gk == G_O ? p.ssq_h : p.ssq_x)[(col >> 5) * BM + row] = sq;
+              if (valid && (et & 3) == 0) (gk == G_O ? p.ssq_h : p.ssq_x)[(col >> 5) * BM + row] = sq;
             }
           }
+          if (et == 0) TK_TRACE(s, EV_RED);
           ++n_gemm;
         }
         arrive(s);
@@ -681,8 +791,7 @@ __global__ void __launch_bounds__(THREADS, 1) stack_kernel(const __grid_constant
     const int sn = norm_stage(L);
     if (static_cast<int>(blockIdx.x) < p.m) depend(sn - 1);
     for (int r = blockIdx.x; ok && r < p.m; r += grid) {
-      float t = 0.f;
-      for (int i = 0; i < parts; ++i) t += __ldcg(p.ssq_x + i * BM + r);
+      const float t = row_ssq(p.ssq_x, parts, r);
       const float rs = rsqrtf(t * (1.0f / static_cast<float>(H)) + p.final_eps);
       for (int c0 = et * 8; c0 < H; c0 += EPI_THREADS * 8) {
         float v[8], w[8];
@@ -1009,6 +1118,15 @@ extern "C" int tk_stack_plan(void* scratch, int* out, int n) {
     out[4 * i + 3] = p.g[i].num_kb;
   }
   if (n > 16) out[16] = it->second.grid;
+  return TK_OK;
+}
+
+extern "C" int tk_stack_trace(void* scratch, unsigned long long* trace) {
+  using namespace tk::stack;
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_plans.find(scratch);
+  if (it == g_plans.end()) return fail_invalid("stack: scratch was not prepared by tk_stack_setup");
+  it->second.p.trace = trace;
   return TK_OK;
 }
 
