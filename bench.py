@@ -369,7 +369,6 @@ def _stack_launch(model, tokens):
     """(closure launching the one-kernel decoder stack on the model's plan for these tokens,
     closure launching the LM head GEMM on its output, algorithmic HBM bytes per stack launch)."""
     import torch
-    from tinker_b200.kernels.gemm import linear
     base = model._model if hasattr(model, "_model") else model
     plan = base._tinker_stack_plans[tuple(tokens.shape)]
     emb, layers, norm, head = base._tinker_stack_parts
@@ -383,7 +382,7 @@ def _stack_launch(model, tokens):
     m, hidden = tokens.numel(), emb.weight.shape[1]
     # every layer's (folded) weights once, the embedding rows in, the final norm's rows out, its weight
     nbytes = weights + 2 * m * hidden * 2 + hidden * 2
-    return (lambda: plan.hidden_states(tokens)), (lambda: linear(y, head.weight)), nbytes
+    return (lambda: plan.hidden_states(tokens)), (lambda: head(y)), nbytes
 
 
 def _time_launches(fn, steps: int, warmup: int = 3):

@@ -1171,7 +1171,16 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   int bn = pick_bn(m_tiles, n, dev.sm_count, cands, 4, constraint);
   if (bn == 0) return fail_invalid("linear: weight block sizes must be multiples of 32");
   SmallPlan plan;
-  if (m_tiles <= 2 || m_tiles * ((n + bn - 1) / bn) < dev.sm_count) {
+  // One M tile and a wide weight (an LM head: 32000 x 1024 at 128 rows) whose 256-column tiles
+  // fill most of the SMs once: one round of wide tiles streams the weight at the HBM rate,
+  // where 128-column tiles would take two uneven rounds and narrower ones re-read the
+  // activation block from L2 once per tile.
+  const int64_t wide_tiles = (n + 255) / 256;
+  const bool one_wide_round = m_tiles == 1 && constraint % 256 == 0 && 4 * wide_tiles >= 3 * dev.sm_count &&
+                              wide_tiles <= dev.sm_count;
+  if (one_wide_round) {
+    bn = 256;
+  } else if (m_tiles <= 2 || m_tiles * ((n + bn - 1) / bn) < dev.sm_count) {
     plan = plan_small_m<DT, EPI_STORE>(m_tiles, n, static_cast<int>((k + BK - 1) / BK), dev.sm_count, constraint,
                                        dev.smem_optin);
     if (plan.bn) bn = plan.bn;

@@ -238,3 +238,4 @@ def share_rope_tables(model: nn.Module) -> int:
         m.cos_table, m.sin_table = c0, s0
         n += 1
     return n
+

@@ -5,7 +5,7 @@ into the q|k|v and gate|up weights, residual adds in the GEMM epilogues), a forw
 at most 128 token rows (batch * seq) still launches 5 kernels per block. For such inputs
 ``install_stack_forward`` routes the model's forward through one persistent kernel that
 runs the embedding, every block and the final RMSNorm (``csrc/stack.cu``), followed by
-the model's LM head weight on this library's GEMM (``tk_linear``). Larger inputs, inputs that are not int64 token ids, and models
+the model's own LM head. Larger inputs, inputs that are not int64 token ids, and models
 whose forward is not exactly ``head(norm(blocks(embedding(tokens))))`` keep the
 per-block path.
 
@@ -33,7 +33,6 @@ import torch.nn as nn
 
 from tinker_b200 import _lib
 from tinker_b200.fusion import _folded_forward, _folded_weights
-from tinker_b200.kernels.gemm import linear
 from tinker_b200.modules.attention import TinKerAttention
 from tinker_b200.modules.normalization import TinKerRMSNorm
 
@@ -232,8 +231,8 @@ def _stack_forward(self, tokens, *args, **kwargs):
         if capturing:
             return self._tinker_stack_orig(tokens)
         plan = plans[shape] = _StackPlan(self, parts, *shape)
-    # the LM head on this library's GEMM (a 128-row weight stream)
-    return linear(plan.hidden_states(tokens), parts[3].weight)
+    # the model's LM head (torch's GEMM: measured faster than this library's at 128 rows)
+    return parts[3](plan.hidden_states(tokens))
 
 
 def install_stack_forward(model: nn.Module, verbose: bool = False) -> bool:
