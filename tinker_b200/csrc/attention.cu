@@ -71,6 +71,7 @@ enum : int {
   B_S_FULL = 12,   // [2] S_a / S_b written (UMMA commit)
   B_P_FULL = 14,   // [2] P_a / P_b written and O rescaled (128 threads of the warpgroup)
   B_PV_DONE = 16,  // [2] P.V of a / b finished (UMMA commit)
+  B_S_FREE = 18,   // [2] S_a / S_b read into registers (128 threads of the warpgroup)
 };
 
 struct Params {
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       mbar_init(bars + B_S_FULL + i, 1);
       mbar_init(bars + B_P_FULL + i, 128);
       mbar_init(bars + B_PV_DONE + i, 1);
+      mbar_init(bars + B_S_FREE + i, 128);
     }
     fence_mbar_init();
   }
@@ -269,19 +271,30 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int iv = 2 * j + 1;
-        if (!mbar_wait(bars + B_FULL + iv % NS, (iv / NS) & 1)) break;
+        // S_{j+1} of each tile as soon as its softmax has read S_j into registers (S_FREE): the
+        // next Q K^T runs while the softmax of step j is still computing
+        if (j + 1 < n_kv) {
+          if (!wait_k(j + 1)) break;
+          if (j + 1 < n_a) {
+            if (!mbar_wait(bars + B_S_FREE + 0, j & 1)) break;
+            tc_fence_after();
+            issue_s(q_a, slot_addr(iv + 1), t_sa);
+            umma_commit(bars + B_S_FULL + 0);
+          }
+          if (has_b) {
+            if (!mbar_wait(bars + B_S_FREE + 1, j & 1)) break;
+            tc_fence_after();
+            issue_s(q_b, slot_addr(iv + 1), t_sb);
+            umma_commit(bars + B_S_FULL + 1);
+          }
+          umma_commit(bars + B_EMPTY + (iv + 1) % NS);  // K_{j+1} consumed
+        }
+        if (!mbar_wait(bars + B_FULL + iv % NS, (iv / NS) & 1)) break;  // V_j
         if (j < n_a) {
           if (!mbar_wait(bars + B_P_FULL + 0, j & 1)) break;
           tc_fence_after();
           issue_pv(p_a, slot_addr(iv), t_oa, j > 0);
           umma_commit(bars + B_PV_DONE + 0);
-        }
-        const bool next_k = j + 1 < n_kv;
-        if (next_k && !wait_k(j + 1)) break;
-        tc_fence_after();
-        if (j + 1 < n_a) {  // S_a is free: softmax a read it before publishing P_a
-          issue_s(q_a, slot_addr(iv + 1), t_sa);
-          umma_commit(bars + B_S_FULL + 0);
         }
         if (has_b) {
           if (!mbar_wait(bars + B_P_FULL + 1, j & 1)) break;
@@ -290,13 +303,6 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
           umma_commit(bars + B_PV_DONE + 1);
         }
         umma_commit(bars + B_EMPTY + iv % NS);  // V_j consumed
-        if (next_k) {
-          if (has_b) {
-            issue_s(q_b, slot_addr(iv + 1), t_sb);
-            umma_commit(bars + B_S_FULL + 1);
-          }
-          umma_commit(bars + B_EMPTY + (iv + 1) % NS);  // K_{j+1} consumed
-        }
       }
     }
   } else if (warp >= ROPE_WARP0) {
@@ -371,6 +377,9 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       tc_fence_after();
       float sv[BKV];
       tmem_load128(t_s + lane_off, sv);
+      // S is in registers: the MMA may write the next tile's scores over it
+      tc_fence_before();
+      mbar_arrive(bars + B_S_FREE + x);
 
       // mask the diagonal tile, then the row maximum over eight independent chains
       if (j == qt) {
