@@ -242,3 +242,16 @@ def test_benchmark_model_reports_the_reference_keys():
     assert r["device"] == "cpu"
     assert 0 <= r["min_ms"] <= r["median_ms"]
     assert r["tokens_per_sec"] == pytest.approx(32 / (r["median_ms"] / 1e3), rel=0.05, abs=1)
+
+
+def test_reference_import_paths_resolve_to_this_package():
+    """Code written against the reference imports `tinker` and its submodules by path."""
+    import tinker
+    from tinker.kernels import fused_attention, fused_rmsnorm, fused_swiglu, precompute_rope_tables  # noqa: F401
+    from tinker.kernels.fused_rmsnorm import fused_rmsnorm as fr
+    from tinker.modules import TinKerAttention as TA
+    from tinker.modules.feed_forward import TinKerSwiGLU as TS
+    from tinker.patch import patch_model as pm
+    from tinker.optimize import benchmark_model as bm
+    assert tinker.optimize is tinker_b200.optimize and pm is tinker_b200.patch_model
+    assert fr is fused_rmsnorm and TA is TinKerAttention and TS is TinKerSwiGLU and bm is tinker_b200.benchmark_model
