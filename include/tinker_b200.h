@@ -248,7 +248,15 @@ TK_API int tk_decode_step_release(void* scratch);
  *                 them): the first weight tiles are then loaded into shared memory before the
  *                 previous kernel has finished (programmatic dependent launch). With 0 they are
  *                 only prefetched into L2 until it has.
+ *  l2_prefetch, l2_prefetch_bytes  up to TK_L2_PREFETCH_MAX device byte ranges (NULL / 0 =
+ *                 unused) that the launch pulls into L2 for the kernels enqueued after it, e.g.
+ *                 the weights of a decoder block's later projections: every CTA issues a share
+ *                 at its start, so their streams start from L2 instead of HBM while the launch
+ *                 chain keeps HBM mostly idle. A hint only: nothing is written, each range is
+ *                 rounded inward to 16-byte boundaries, and the ranges must stay allocated until
+ *                 the launch has finished.
  */
+#define TK_L2_PREFETCH_MAX 8
 typedef struct tk_epilogue {
   const void* residual;
   const float* row_ssq_in;
@@ -262,6 +270,8 @@ typedef struct tk_epilogue {
   const void* rope_sin;
   int64_t rope_table_rows;
   int weights_prefetch;
+  const void* l2_prefetch[TK_L2_PREFETCH_MAX];
+  int64_t l2_prefetch_bytes[TK_L2_PREFETCH_MAX];
 } tk_epilogue;
 
 /*

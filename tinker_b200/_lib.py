@@ -31,7 +31,7 @@ class Epilogue(ctypes.Structure):
     _fields_ = [("residual", _P), ("row_ssq_in", _P), ("row_ssq_parts", _I), ("row_ssq_eps", _F),
                 ("row_ssq_out", _P), ("rope_seq", _I), ("rope_start", _I), ("rope_head_dim", _I),
                 ("rope_cos", _P), ("rope_sin", _P), ("rope_table_rows", _I64),
-                ("weights_prefetch", _I)]
+                ("weights_prefetch", _I), ("l2_prefetch", _P * 8), ("l2_prefetch_bytes", _I64 * 8)]
 
 
 _EPI = ctypes.POINTER(Epilogue)

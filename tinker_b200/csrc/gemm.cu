@@ -68,6 +68,7 @@ struct Params {
   // Nonzero: no kernel since the stream last waited for all earlier work wrote the weights,
   // so their first tiles may go to shared memory before griddepcontrol.wait.
   int weights_prefetch;
+  L2Prefetch pf;  // weights of later kernels pulled into L2 (every CTA a share, at its start)
 };
 
 // 1/rms of input row `row` for a folded RMSNorm (1 when there is none or the row is padding).
@@ -267,6 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == 3 && p.pf.n) l2_prefetch_share(p.pf, blockIdx.x, gridDim.x, lane);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -489,6 +491,7 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA signal
   if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == 3 && p.pf.n) l2_prefetch_share(p.pf, blockIdx.x, gridDim.x, lane);
 
   if (warp == 0) {
     if (elect_one()) {
@@ -709,6 +712,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   cluster_sync();  // every CTA of the cluster is running before any remote shared-memory write
   if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == 3 && p.pf.n)
+    l2_prefetch_share(p.pf, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
+                      gridDim.x * gridDim.y * gridDim.z, lane);
 
   if (warp == 0) {
     if (elect_one()) {
@@ -1014,6 +1020,7 @@ int launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorM
 
 // Tile plan for problems with few output tiles: split K over a cluster of `split`
 // CTAs when that keeps all CTAs in one wave and cuts the bytes each CTA must pull.
+constexpr int DEEP_STAGES = 8;  // ring of the single-wave plain kernel (see plan_small_m)
 struct SmallPlan {
   int bn = 0, split = 1, stages = 4;
 };
@@ -1067,9 +1074,10 @@ static int max_active_clusters(int bn, int split, int smem) {
 // ~1.8 of set-up and first-load latency, the CTA's k-slice of activations plus
 // weights at ~100 GB/s per SM (shared by the CTAs an SM holds), and for split > 1
 // a DSMEM reduction of ~0.8 + (partial bytes sent) / 25 GB/s; the owner epilogue
-// grows with BN. Split-K plans must fit in one wave of co-resident clusters;
-// rings are kept at <= 4 stages so that two CTAs can share an SM. Splits stay
-// <= 4 and BN <= 64 (beyond that the reduction and cluster barriers dominate).
+// grows with BN. Split-K plans must fit in one wave of co-resident clusters,
+// costed with <= 4-stage rings (two CTAs per SM); a plan of one CTA per SM then
+// gets a deep ring (below). Splits stay <= 4 and BN <= 64 (beyond that the
+// reduction and cluster barriers dominate).
 template <int DT, int EPI>
 static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sms, int64_t constraint,
                               size_t smem_cap) {
@@ -1106,6 +1114,24 @@ static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sm
       }
     }
   }
+  // One wave with one CTA per SM: a deep ring. At a few hundred rows every k-block's TMA
+  // round trip (L2 latency under load, ~1.5 us) costs more than its transfer, so the CTA's
+  // stream runs in ceil(k-blocks / stages) round trips; 8 stages halve them against 4 (a
+  // CTA then fills its SM's shared memory, so the next kernel's CTA no longer starts beside it).
+  if (best.bn) {
+    const int64_t tiles = m_tiles * ((n_out + (swiglu ? best.bn / 2 : best.bn) - 1) / (swiglu ? best.bn / 2 : best.bn));
+    const int kb_per_cta = (num_kb + best.split - 1) / best.split;
+    if (tiles * best.split <= sms && kb_per_cta > best.stages) {
+      const int deep = std::min(SplitSmem<32>::MAX_STAGES, kb_per_cta);
+      if (best.split == 1) {
+        best.stages = DEEP_STAGES;
+      } else if (static_cast<size_t>(splitk_smem(best.bn, best.split, deep)) <= smem_cap &&
+                 max_active_clusters<DT, EPI>(best.bn, best.split, splitk_smem(best.bn, best.split, deep)) >=
+                     m_tiles * ((n_out + (swiglu ? best.bn / 2 : best.bn) - 1) / (swiglu ? best.bn / 2 : best.bn))) {
+        best.stages = deep;
+      }
+    }
+  }
   return best;
 }
 
@@ -1134,6 +1160,7 @@ struct Extras {
   float ssq_inv_k = 0.f, ssq_eps = 0.f;
   float* ssq_out = nullptr;
   int weights_prefetch = 0;
+  L2Prefetch pf{};
 };
 
 void apply_extras(Params& p, const Extras& e) {
@@ -1150,6 +1177,7 @@ void apply_extras(Params& p, const Extras& e) {
   p.ssq_eps = e.ssq_eps;
   p.ssq_out = e.ssq_out;
   p.weights_prefetch = e.weights_prefetch;
+  p.pf = e.pf;
 }
 
 template <int DT>
@@ -1239,8 +1267,12 @@ int run_linear(const void* x, int64_t lda, const void* w0, int64_t n0, const voi
   switch (bn) {
     case 256: return launch<DT, 256, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 1, st);
     case 128: return launch<DT, 128, EPI_STORE, 5>(ta, tb0, tb1, tb2, p, 1, st);
-    case 64: return launch<DT, 64, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
-    default: return launch<DT, 32, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
+    case 64:
+      if (plan.stages == DEEP_STAGES) return launch<DT, 64, EPI_STORE, DEEP_STAGES>(ta, tb0, tb1, tb2, p, 1, st);
+      return launch<DT, 64, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
+    default:
+      if (plan.stages == DEEP_STAGES) return launch<DT, 32, EPI_STORE, DEEP_STAGES>(ta, tb0, tb1, tb2, p, 1, st);
+      return launch<DT, 32, EPI_STORE, 4>(ta, tb0, tb1, tb2, p, 2, st);
   }
 }
 
@@ -1313,8 +1345,12 @@ int run_gate_up(const void* x, int64_t lda, const void* wg, const void* wu, void
   switch (half) {
     case 128: return launch<DT, 256, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 1, st);
     case 64: return launch<DT, 128, EPI_SWIGLU, 5>(ta, tg, tu, tu, p, 1, st);
-    case 32: return launch<DT, 64, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
-    default: return launch<DT, 32, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
+    case 32:
+      if (plan.stages == DEEP_STAGES) return launch<DT, 64, EPI_SWIGLU, DEEP_STAGES>(ta, tg, tu, tu, p, 1, st);
+      return launch<DT, 64, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
+    default:
+      if (plan.stages == DEEP_STAGES) return launch<DT, 32, EPI_SWIGLU, DEEP_STAGES>(ta, tg, tu, tu, p, 1, st);
+      return launch<DT, 32, EPI_SWIGLU, 4>(ta, tg, tu, tu, p, 2, st);
   }
 }
 
@@ -1332,6 +1368,8 @@ static int check_gemm_common(int dtype, const void* x, int64_t lda, int64_t m, i
   if (m > 0x7fffffffLL || k > 0x7fffffffLL) return fail_invalid("GEMM: size too large");
   return TK_OK;
 }
+
+static_assert(L2_PF_MAX == TK_L2_PREFETCH_MAX, "tk_epilogue prefetch slots");
 
 namespace {
 
@@ -1354,6 +1392,7 @@ int extras_from(const tk_epilogue* e, int64_t m, int64_t k, int64_t n, int64_t r
     ex->ssq_out = e->row_ssq_out;
   }
   ex->weights_prefetch = e->weights_prefetch ? 1 : 0;
+  l2_prefetch_from(e->l2_prefetch, e->l2_prefetch_bytes, &ex->pf);
   if (e->rope_head_dim) {
     const int hd = e->rope_head_dim;
     if (!plain_store || hd < 32 || hd % 32 != 0 || rope_cols % hd != 0 || rope_cols > n)

@@ -197,6 +197,57 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int32_t x,
                "r"(x), "r"(y)
                : "memory");
 }
+// Pull [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16). A hint: it writes
+// no memory this grid reads and waits for nothing, so it may run before griddepcontrol.wait.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
+
+// Byte ranges a kernel pulls into L2 for the kernels launched after it (the weights of the
+// next projections of a decoder block), so that their weight streams start from L2 instead of
+// HBM: the launch chain leaves HBM mostly idle, and these ranges never depend on the previous
+// kernel (a later write still lands in L2, the point of coherence), so every CTA issues its
+// share at its start. The host rounds each range inward to 16-byte boundaries.
+constexpr int L2_PF_MAX = 8;
+struct L2Prefetch {
+  const char* base[L2_PF_MAX];
+  int64_t bytes[L2_PF_MAX];
+  int n;
+};
+
+// The ranges of a tk_epilogue (NULL pointer or size <= 0: unused slot), each rounded inward
+// to 16-byte boundaries; ranges left empty are dropped.
+inline void l2_prefetch_from(const void* const* ptrs, const int64_t* bytes, L2Prefetch* out) {
+  *out = L2Prefetch{};
+  for (int i = 0; i < L2_PF_MAX; ++i) {
+    if (!ptrs[i] || bytes[i] <= 0) continue;
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(ptrs[i]) + 15) & ~uintptr_t(15);
+    const uintptr_t hi = (reinterpret_cast<uintptr_t>(ptrs[i]) + static_cast<uintptr_t>(bytes[i])) & ~uintptr_t(15);
+    if (hi <= lo) continue;
+    out->base[out->n] = reinterpret_cast<const char*>(lo);
+    out->bytes[out->n] = static_cast<int64_t>(hi - lo);
+    ++out->n;
+  }
+}
+
+// This CTA's share of `pf`: each range is cut into 32 KB chunks, chunk g of the concatenation
+// goes to CTA g % ctas, and the lanes of the calling warp issue the CTA's chunks.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int ctas, int lane) {
+  constexpr int64_t CHUNK = 32768;
+  int64_t first = 0;  // index of the range's first chunk in the concatenation
+  for (int r = 0; r < pf.n && r < L2_PF_MAX; ++r) {
+    const int64_t bytes = pf.bytes[r];
+    const int64_t nchunks = (bytes + CHUNK - 1) / CHUNK;
+    const int64_t g0 = first + ((cta - first % ctas) % ctas + ctas) % ctas;
+    for (int64_t g = g0 + static_cast<int64_t>(lane) * ctas; g < first + nchunks; g += 32ll * ctas) {
+      const int64_t off = (g - first) * CHUNK;
+      bulk_prefetch_l2(pf.base[r] + off, static_cast<uint32_t>(min(CHUNK, bytes - off)));
+    }
+    first += nchunks;
+  }
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }

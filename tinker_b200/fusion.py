@@ -42,6 +42,7 @@ from __future__ import annotations
 
 import inspect
 import types
+import weakref
 
 import torch
 import torch.nn as nn
@@ -139,17 +140,53 @@ def _folded_forward(self, x: torch.Tensor, kv_cache=None, start_pos: int = 0,
         a = at.cached_attention(x, wq, wk, wv, kv_cache, start_pos, position, row_ssq_in=ssq_x,
                                 row_ssq_eps=n1.eps)
     else:
+        # the q|k|v launch pulls the block's other weights into L2 (see _ahead_weights)
         qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
-                          row_ssq_eps=n1.eps)
+                          row_ssq_eps=n1.eps, l2_prefetch=(at.o_proj.weight, wg, wu, ff.down_proj.weight))
         a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
                              at.num_kv_heads, at.head_dim)
     ssq_h = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
-    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h)
+    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h,
+               l2_prefetch=_ahead_weights(self) if kv_cache is None else None)
     g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)
     ssq_y = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
     y = linear(g, ff.down_proj.weight, residual=h, row_ssq_out=ssq_y)
     y._tinker_row_ssq = (ssq_y, _version_of(y))  # the next folded block reads the statistics from here
     return y
+
+
+_AHEAD_MAX_BYTES = 80 << 20
+
+
+def _ahead_weights(block) -> tuple:
+    """The weights the launches after this block start with: the next fused block's folded
+    q|k|v weights (when it has made them), or the LM head weight after the last block. The
+    o_proj launch pulls them into L2 so that the next block's first GEMM (or the head) streams
+    them from there; the q|k|v launch does the same for the rest of its own block. The launch
+    chain of a forward at a few hundred rows leaves HBM mostly idle, so these reads come free."""
+    ref = block.__dict__.get("_tinker_ahead")
+    nxt = ref() if ref is not None else None
+    if nxt is None:
+        return ()
+    if isinstance(nxt, nn.Linear):
+        w = nxt.weight
+        # a head far larger than a third of L2 (a tied 150k-token table) would not stay there
+        return (w,) if w.numel() * w.element_size() <= _AHEAD_MAX_BYTES else ()
+    cached = nxt.__dict__.get("_tinker_folded")
+    return tuple(cached[1][:3]) if cached is not None else ()
+
+
+def link_ahead(model: nn.Module) -> int:
+    """Record for every fused block which module runs next (the next fused block in module
+    order, and after the last one the model's ``output`` / ``lm_head`` Linear if it has one),
+    for the L2 prefetch of ``_ahead_weights``. A wrong guess costs bandwidth, never results."""
+    blocks = [m for m in model.modules() if getattr(m, "_tinker_block_parts", None) is not None]
+    head = next((h for h in (getattr(model, n, None) for n in ("output", "lm_head")) if isinstance(h, nn.Linear)),
+                None)
+    for i, b in enumerate(blocks):
+        nxt = blocks[i + 1] if i + 1 < len(blocks) else head
+        b.__dict__["_tinker_ahead"] = weakref.ref(nxt) if nxt is not None else None
+    return len(blocks)
 
 
 def _dataflow_is_prenorm_residual(block: nn.Module, parts, x: torch.Tensor, gen) -> bool:
@@ -215,6 +252,8 @@ def fuse_decoder_blocks(model: nn.Module, verbose: bool = False, probe_tokens: i
         fused += 1
         if verbose:
             print(f"  [tinker] fused decoder block {name}")
+    if fused:
+        link_ahead(model)
     return fused
 
 

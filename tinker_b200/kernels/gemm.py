@@ -41,13 +41,17 @@ def _check_x(x: torch.Tensor) -> torch.Tensor:
     return x2
 
 
-def _epilogue(residual=None, row_ssq_in=None, row_ssq_eps=1e-6, row_ssq_out=None, rope=None):
+def _epilogue(residual=None, row_ssq_in=None, row_ssq_eps=1e-6, row_ssq_out=None, rope=None, l2_prefetch=None):
     """A ``tk_epilogue`` for the ``_ex`` entry points (None when only the plain store is needed)."""
     stable = weights_are_stable()
-    if residual is None and row_ssq_in is None and row_ssq_out is None and rope is None and not stable:
+    pf = [t for t in (l2_prefetch or ()) if t is not None and t.is_cuda and t.is_contiguous() and t.numel()]
+    if residual is None and row_ssq_in is None and row_ssq_out is None and rope is None and not stable and not pf:
         return None
     e = _lib.Epilogue()
     e.weights_prefetch = 1 if stable else 0
+    for i, t in enumerate(pf[:len(e.l2_prefetch)]):
+        e.l2_prefetch[i] = t.data_ptr()
+        e.l2_prefetch_bytes[i] = t.numel() * t.element_size()
     e.residual = None if residual is None else residual.data_ptr()
     if row_ssq_in is not None:
         if row_ssq_in.dtype != torch.float32 or row_ssq_in.dim() != 2 or not row_ssq_in.is_contiguous():
@@ -90,13 +94,15 @@ def row_sumsq(x: torch.Tensor) -> torch.Tensor:
 def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
            row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,
-           row_ssq_out: torch.Tensor | None = None) -> torch.Tensor:
+           row_ssq_out: torch.Tensor | None = None, l2_prefetch=None) -> torch.Tensor:
     """``x @ cat([w0, w1, w2]).T (+ residual)``; x [..., k], w* [n*, k].
 
     ``row_ssq_in`` ([parts, m] float32, from ``row_sumsq`` or another GEMM's ``row_ssq_out``) scales
     each output row by ``1/sqrt(mean(x_row^2) + row_ssq_eps)``: with an RMSNorm weight folded into
     the weights this is ``rmsnorm(x) @ W.T``. ``row_ssq_out`` ([ceil(n/32), m] float32) receives the
-    partial sums of squares of the stored rows for the next folded RMSNorm."""
+    partial sums of squares of the stored rows for the next folded RMSNorm. ``l2_prefetch``: up to
+    8 contiguous device tensors (the weights of the kernels that follow) that the launch pulls
+    into L2 while it runs; they must stay alive until it has finished."""
     ws = [w for w in (w0, w1, w2) if w is not None]
     dev = _lib.require_cuda(x, *ws)
     x2 = _check_x(x)
@@ -118,7 +124,7 @@ def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2
     _check_ssq(row_ssq_out, m, (n + 31) // 32, "row_ssq_out")
     ptrs = [w.data_ptr() for w in ws] + [None] * (3 - len(ws))
     rows = [w.shape[0] for w in ws] + [0] * (3 - len(ws))
-    e = _epilogue(r, row_ssq_in, row_ssq_eps, row_ssq_out)
+    e = _epilogue(r, row_ssq_in, row_ssq_eps, row_ssq_out, l2_prefetch=l2_prefetch)
     with call_ctx(dev):
         if e is None:
             _lib.check(_lib.lib().tk_linear(x2.data_ptr(), row_stride(x2), ptrs[0], rows[0], ptrs[1], rows[1], ptrs[2],
@@ -133,11 +139,13 @@ def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2
 
 def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, cos_table: torch.Tensor,
                 sin_table: torch.Tensor, head_dim: int, start_pos: int = 0,
-                row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
+                row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,
+                l2_prefetch=None) -> torch.Tensor:
     """``x @ cat([wq, wk, wv]).T`` for x [batch, seq, hidden] with RoPE applied to the q and k
     columns in the GEMM epilogue (each value rounded to the output dtype, then rotated in fp32 at
     position ``start_pos + s``): the q|k|v projection plus the RoPE of ``fused_attention``.
-    ``row_ssq_in`` / ``row_ssq_eps`` as in ``linear`` (the attention RMSNorm folded in)."""
+    ``row_ssq_in`` / ``row_ssq_eps`` / ``l2_prefetch`` as in ``linear`` (the attention RMSNorm
+    folded in)."""
     dev = _lib.require_cuda(x, wq, wk, wv, cos_table, sin_table)
     if x.dim() != 3:
         raise ValueError("linear_rope: x must be [batch, seq, hidden]")
@@ -154,7 +162,7 @@ def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.T
     _check_ssq(row_ssq_in, m, None, "row_ssq_in")
     out = torch.empty(m, n, dtype=x.dtype, device=x.device)
     with call_ctx(dev):
-        if row_ssq_in is None and not weights_are_stable():
+        if row_ssq_in is None and not weights_are_stable() and not l2_prefetch:
             _lib.check(_lib.lib().tk_linear_rope(
                 x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0],
                 wv.data_ptr(), wv.shape[0], out.data_ptr(), n, m, k, S, int(start_pos), head_dim, c.data_ptr(),
@@ -162,7 +170,7 @@ def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.T
         else:
             if wq.shape[0] % head_dim or wk.shape[0] % head_dim:
                 raise ValueError("linear_rope: q and k widths must be multiples of head_dim")
-            e = _epilogue(None, row_ssq_in, row_ssq_eps, None, (c, s_, head_dim, S, start_pos))
+            e = _epilogue(None, row_ssq_in, row_ssq_eps, None, (c, s_, head_dim, S, start_pos), l2_prefetch)
             _lib.check(_lib.lib().tk_linear_ex(
                 x2.data_ptr(), row_stride(x2), wq.data_ptr(), wq.shape[0], wk.data_ptr(), wk.shape[0],
                 wv.data_ptr(), wv.shape[0], out.data_ptr(), n, m, k, e, _lib.dtype_code(x.dtype),
@@ -171,9 +179,10 @@ def linear_rope(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.T
 
 
 def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
-                   row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
+                   row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,
+                   l2_prefetch=None) -> torch.Tensor:
     """``silu(x @ w_gate.T) * (x @ w_up.T)`` as one GEMM with a SwiGLU epilogue; ``row_ssq_in`` /
-    ``row_ssq_eps`` as in ``linear`` (the FFN RMSNorm folded into both weights)."""
+    ``row_ssq_eps`` / ``l2_prefetch`` as in ``linear`` (the FFN RMSNorm folded into both weights)."""
     dev = _lib.require_cuda(x, w_gate, w_up)
     x2 = _check_x(x)
     k = x2.shape[1]
@@ -184,7 +193,7 @@ def gate_up_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     m = x2.shape[0]
     _check_ssq(row_ssq_in, m, None, "row_ssq_in")
     h = torch.empty(m, f, dtype=x.dtype, device=x.device)
-    e = _epilogue(None, row_ssq_in, row_ssq_eps)
+    e = _epilogue(None, row_ssq_in, row_ssq_eps, l2_prefetch=l2_prefetch)
     with call_ctx(dev):
         if e is None:
             _lib.check(_lib.lib().tk_gate_up_swiglu(x2.data_ptr(), row_stride(x2), wg.data_ptr(), wu.data_ptr(),
