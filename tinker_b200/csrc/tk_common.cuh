@@ -14,6 +14,7 @@
 #include <stdint.h>
 
 #include "../../include/tinker_b200.h"
+#include "tk_host.h"
 
 #ifndef TK_WAIT_LIMIT_NS
 #define TK_WAIT_LIMIT_NS 2000000000ull  // 2 s
@@ -202,33 +203,6 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int32_t x,
 __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
                : "memory");
-}
-
-// Byte ranges a kernel pulls into L2 for the kernels launched after it (the weights of the
-// next projections of a decoder block), so that their weight streams start from L2 instead of
-// HBM: the launch chain leaves HBM mostly idle, and these ranges never depend on the previous
-// kernel (a later write still lands in L2, the point of coherence), so every CTA issues its
-// share at its start. The host rounds each range inward to 16-byte boundaries.
-constexpr int L2_PF_MAX = 8;
-struct L2Prefetch {
-  const char* base[L2_PF_MAX];
-  int64_t bytes[L2_PF_MAX];
-  int n;
-};
-
-// The ranges of a tk_epilogue (NULL pointer or size <= 0: unused slot), each rounded inward
-// to 16-byte boundaries; ranges left empty are dropped.
-inline void l2_prefetch_from(const void* const* ptrs, const int64_t* bytes, L2Prefetch* out) {
-  *out = L2Prefetch{};
-  for (int i = 0; i < L2_PF_MAX; ++i) {
-    if (!ptrs[i] || bytes[i] <= 0) continue;
-    const uintptr_t lo = (reinterpret_cast<uintptr_t>(ptrs[i]) + 15) & ~uintptr_t(15);
-    const uintptr_t hi = (reinterpret_cast<uintptr_t>(ptrs[i]) + static_cast<uintptr_t>(bytes[i])) & ~uintptr_t(15);
-    if (hi <= lo) continue;
-    out->base[out->n] = reinterpret_cast<const char*>(lo);
-    out->bytes[out->n] = static_cast<int64_t>(hi - lo);
-    ++out->n;
-  }
 }
 
 // This CTA's share of `pf`: each range is cut into 32 KB chunks, chunk g of the concatenation

@@ -83,6 +83,33 @@ int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, 
 int tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d0, uint64_t d1, uint64_t d2,
                   uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
 
+// Byte ranges a kernel pulls into L2 for the kernels launched after it (the weights of the
+// next projections of a decoder block), so that their weight streams start from L2 instead of
+// HBM: the launch chain leaves HBM mostly idle, and these ranges never depend on the previous
+// kernel (a later write still lands in L2, the point of coherence), so every CTA issues its
+// share at its start. The host rounds each range inward to 16-byte boundaries.
+constexpr int L2_PF_MAX = 8;
+struct L2Prefetch {
+  const char* base[L2_PF_MAX];
+  int64_t bytes[L2_PF_MAX];
+  int n;
+};
+
+// The ranges of a tk_epilogue (NULL pointer or size <= 0: unused slot), each rounded inward
+// to 16-byte boundaries; ranges left empty are dropped.
+inline void l2_prefetch_from(const void* const* ptrs, const int64_t* bytes, L2Prefetch* out) {
+  *out = L2Prefetch{};
+  for (int i = 0; i < L2_PF_MAX; ++i) {
+    if (!ptrs[i] || bytes[i] <= 0) continue;
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(ptrs[i]) + 15) & ~uintptr_t(15);
+    const uintptr_t hi = (reinterpret_cast<uintptr_t>(ptrs[i]) + static_cast<uintptr_t>(bytes[i])) & ~uintptr_t(15);
+    if (hi <= lo) continue;
+    out->base[out->n] = reinterpret_cast<const char*>(lo);
+    out->bytes[out->n] = static_cast<int64_t>(hi - lo);
+    ++out->n;
+  }
+}
+
 // Weight-streaming products for 1..MAX_M rows (gemv.cu): y = x W^T over up to three weight
 // blocks stacked along n (nrows[i] rows each, w[i] null when absent), with the GEMM epilogue
 // options, or SwiGLU of gate w[0] and up w[1] (n output columns). Used by the GEMM entry points
@@ -91,7 +118,7 @@ namespace gemv {
 constexpr int MAX_M = 8;
 int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int64_t nrows[3], bool swiglu, void* y,
         int64_t ldy, int64_t m, int64_t n, int64_t k, const void* residual, const float* ssq_in, int ssq_parts,
-        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st);
+        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st, const L2Prefetch* pf = nullptr);
 }  // namespace gemv
 
 }  // namespace tk

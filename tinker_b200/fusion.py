@@ -136,18 +136,19 @@ def _folded_forward(self, x: torch.Tensor, kv_cache=None, start_pos: int = 0,
     if ssq_x is None:
         ssq_x = row_sumsq(x)
     hq, hkv = at.num_heads * at.head_dim, at.num_kv_heads * at.head_dim
+    # the q|k|v launch pulls the block's other weights into L2, the o_proj launch those of
+    # whatever runs next (see _ahead_weights)
+    later = (at.o_proj.weight, wg, wu, ff.down_proj.weight)
     if kv_cache is not None:
         a = at.cached_attention(x, wq, wk, wv, kv_cache, start_pos, position, row_ssq_in=ssq_x,
-                                row_ssq_eps=n1.eps)
+                                row_ssq_eps=n1.eps, l2_prefetch=later)
     else:
-        # the q|k|v launch pulls the block's other weights into L2 (see _ahead_weights)
         qkv = linear_rope(x, wq, wk, wv, at.cos_table, at.sin_table, at.head_dim, 0, row_ssq_in=ssq_x,
-                          row_ssq_eps=n1.eps, l2_prefetch=(at.o_proj.weight, wg, wu, ff.down_proj.weight))
+                          row_ssq_eps=n1.eps, l2_prefetch=later)
         a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
                              at.num_kv_heads, at.head_dim)
     ssq_h = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
-    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h,
-               l2_prefetch=_ahead_weights(self) if kv_cache is None else None)
+    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h, l2_prefetch=_ahead_weights(self))
     g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)
     ssq_y = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
     y = linear(g, ff.down_proj.weight, residual=h, row_ssq_out=ssq_y)

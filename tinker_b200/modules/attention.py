@@ -94,10 +94,12 @@ class TinKerAttention(nn.Module):
 
     def cached_attention(self, x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, kv_cache,
                          start_pos: int = 0, position: torch.Tensor | None = None,
-                         row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6) -> torch.Tensor:
+                         row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,
+                         l2_prefetch=None) -> torch.Tensor:
         """q|k|v projection of x with the weights given (the module's own, or copies with an
         RMSNorm folded in, ``row_ssq_in``) and attention against ``kv_cache``, which receives the
         new keys and values. Returns the attention output [B, S, num_heads * head_dim].
+        ``l2_prefetch``: tensors the projection launch pulls into L2 (``kernels.gemm.linear``).
 
         A prompt at position 0 with more than ``PROMPT_MIN_ROWS`` query rows per kv head takes the
         tensor-core path (RoPE in the projection epilogue, causal attention, cache append);
@@ -112,12 +114,13 @@ class TinKerAttention(nn.Module):
         groups = self.num_heads // self.num_kv_heads
         norm = {} if row_ssq_in is None else {"row_ssq_in": row_ssq_in, "row_ssq_eps": row_ssq_eps}
         if position is None and int(start_pos) == 0 and groups * S > PROMPT_MIN_ROWS:
-            qkv = linear_rope(x, wq, wk, wv, self.cos_table, self.sin_table, self.head_dim, 0, **norm)
+            qkv = linear_rope(x, wq, wk, wv, self.cos_table, self.sin_table, self.head_dim, 0, **norm,
+                              l2_prefetch=l2_prefetch)
             k, v = qkv[..., hq:hq + hkv], qkv[..., hq + hkv:]
             a = causal_attention(qkv[..., :hq], k, v, self.num_heads, self.num_kv_heads, self.head_dim)
             kv_append(k, v, kv_cache.k, kv_cache.v, 0)
             return a
-        qkv = linear(x, wq, wk, wv, **norm)
+        qkv = linear(x, wq, wk, wv, **norm, l2_prefetch=l2_prefetch)
         return kv_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], self.cos_table,
                             self.sin_table, kv_cache.k, kv_cache.v, self.num_heads, self.num_kv_heads,
                             self.head_dim, start_pos, position, kv_cache.workspace(S))
