@@ -57,6 +57,9 @@ struct Smem {
   static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
   static constexpr int NUM_BARS = 24;
   static constexpr int TOTAL = 1024 + BAR_OFF + NUM_BARS * 8 + 16;
+  // single-tile CTAs (no query tile b): the per-row partial max and sum of the two column
+  // halves, [4][128] fp32, in tile b's Q slot
+  static constexpr int RED_OFF = Q_OFF + Q_BYTES;
   // S_a: 0-127, S_b: 128-255, O_a: 256.., O_b: 256 + head_dim..
   static constexpr uint32_t TMEM_COLS = 512;
 };
@@ -172,6 +175,9 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
   const bool has_b = 2 * blk + 1 < p.n_qtiles;
   const int n_a = 2 * blk + 1;             // key tiles of query tile a (causal)
   const int n_kv = has_b ? n_a + 1 : n_a;  // key tiles loaded (query tile b needs one more)
+  // a sequence of at most 128 rows: one query tile and one key tile per CTA, so both softmax
+  // warpgroups work on it, each on one half of the key columns
+  const bool single = p.n_qtiles == 1;
 
   if (tid == 0) {
     mbar_init(bars + B_Q_FULL, 1);
@@ -183,7 +189,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bars + B_K_READY + i, ROPE_K_THREADS);
       mbar_init(bars + B_S_FULL + i, 1);
-      mbar_init(bars + B_P_FULL + i, 128);
+      mbar_init(bars + B_P_FULL + i, single ? 256 : 128);
       mbar_init(bars + B_PV_DONE + i, 1);
       mbar_init(bars + B_S_FREE + i, 128);
     }
@@ -336,6 +342,104 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(bars + B_K_READY + (j & 1));
+      }
+    }
+  } else if (warp < 8 && single) {
+    // ---------------- one key tile: warpgroup h takes key columns [64 h, 64 h + 64) of row r ----------------
+    const int h2 = warp >> 2;
+    const int r = tid & 127;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float* red = reinterpret_cast<float*>(smem + S::RED_OFF);  // [max h0, max h1, sum h0, sum h1][row]
+    uint8_t* sq = smem + S::Q_OFF;
+    uint8_t* sp = smem + S::P_OFF;
+    bool ok = true;
+    if constexpr (ROPE) {
+      const bool valid = h2 == 0 && r < p.seq;
+      float c[32], sn[32];
+      pdl_wait();  // the tables may have been written by the previous kernel
+      if (valid) rope_load_block(p, static_cast<int64_t>(p.start_pos) + r, 0, D / 2, c, sn);
+      ok = mbar_wait(bars + B_Q_FULL, 0);
+      if (ok && valid) {
+        rope_apply_block<DT>(sq, r, 0, c, sn);
+#pragma unroll
+        for (int cb = 1; cb < D / 64; ++cb) {
+          rope_load_block(p, static_cast<int64_t>(p.start_pos) + r, cb, D / 2, c, sn);
+          rope_apply_block<DT>(sq, r, cb, c, sn);
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(bars + B_Q_READY);
+    ok = ok && mbar_wait(bars + B_S_FULL + 0, 0);
+    tc_fence_after();
+    float sv[64];
+    tmem_load64(tmem_base + lane_off + h2 * 64, sv);
+#pragma unroll
+    for (int c = 0; c < 64; ++c)
+      if (h2 * 64 + c > r) sv[c] = -INFINITY;  // causal mask of the diagonal tile
+    float mx8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+    for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+    red[h2 * BQ + r] = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+    named_sync(1, SOFTMAX_THREADS);
+    // column 0 is never masked, so the row maximum is finite
+    const float neg_m = -fmaxf(red[r], red[BQ + r]) * p.scale_log2;
+    const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), negm2 = pack_f32x2(neg_m, neg_m);
+    uint64_t rs2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 64; c += 2) {
+      const uint64_t e = fma_f32x2(pack_f32x2(sv[c], sv[c + 1]), scale2, negm2);
+      float e0, e1;
+      unpack_f32x2(e, e0, e1);
+      sv[c] = exp2_approx(e0);
+      sv[c + 1] = exp2_approx(e1);
+      rs2[(c >> 1) & 3] = add_f32x2(rs2[(c >> 1) & 3], pack_f32x2(sv[c], sv[c + 1]));
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&hv);
+      }
+      *reinterpret_cast<uint4*>(sp + h2 * (128 * 128) + r * 128 + ((c ^ (r & 7)) * 16)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(bars + B_P_FULL + 0);  // 256 arrivals: both halves of P
+    float rp[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) unpack_f32x2(rs2[i], rp[2 * i], rp[2 * i + 1]);
+    red[(2 + h2) * BQ + r] = ((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7]));
+    named_sync(1, SOFTMAX_THREADS);
+    const float inv_l = 1.0f / (red[2 * BQ + r] + red[3 * BQ + r]);
+    // O / l: warpgroup h2 writes output columns [h2 D/2, h2 D/2 + D/2) of row r
+    if (ok && mbar_wait(bars + B_PV_DONE + 0, 0)) {
+      tc_fence_after();
+      using T = typename Dx::T;
+      T* dst = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.seq + r) * p.out_tok_stride +
+               static_cast<int64_t>(h) * D;
+#pragma unroll
+      for (int c = h2 * (D / 2); c < (h2 + 1) * (D / 2); c += 32) {
+        float o[32];
+        tmem_load32(tmem_base + 256 + lane_off + c, o);
+        if (r < p.seq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              typename Dx::T2 hv = Dx::pack(o[q * 8 + 2 * i] * inv_l, o[q * 8 + 2 * i + 1] * inv_l);
+              w[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            reinterpret_cast<uint4*>(dst + c)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
       }
     }
   } else if (warp < 8) {
