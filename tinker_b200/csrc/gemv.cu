@@ -35,7 +35,6 @@ struct Params {
   float ssq_inv_k, ssq_eps;
   float* ssq_out;  // [ceil(n / 32), m]
   int m, n, k;
-  L2Prefetch pf;  // weights of later kernels pulled into L2 (every CTA a share, at its start)
 };
 
 template <int DT>
@@ -85,7 +84,6 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
       }
     }
   }
-  if (warp == WARPS - 1 && p.pf.n) l2_prefetch_share(p.pf, blockIdx.x, gridDim.x, lane);
   // the weights do not depend on the previous kernel: start pulling them into L2
   for (int r = 0; r < ROWS; ++r)
     if (wrow[r])
@@ -218,7 +216,7 @@ int launch_dt(const Params& p, bool swiglu, int cpw, cudaStream_t st) {
 
 int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int64_t nrows[3], bool swiglu, void* y,
         int64_t ldy, int64_t m, int64_t n, int64_t k, const void* residual, const float* ssq_in, int ssq_parts,
-        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st, const L2Prefetch* pf) {
+        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st) {
   if (m < 1 || m > MAX_M) return fail_invalid("gemv: 1 <= m <= 8 rows");
   if (k % 8 != 0 || lda % 8 != 0 || ldy < 1) return fail_invalid("gemv: k and the row stride must be multiples of 8");
   if (!aligned16(x) || !aligned16(w[0]) || (w[1] && !aligned16(w[1])) || (w[2] && !aligned16(w[2])))
@@ -244,7 +242,6 @@ int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  if (pf) p.pf = *pf;
   // columns per warp: the most that still gives about two CTAs per SM (one with ssq_out, whose
   // 32-column chunks are split over clusters of 4 CTAs)
   const int max_cpw = swiglu ? 2 : 4;

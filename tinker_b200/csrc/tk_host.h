@@ -118,7 +118,7 @@ namespace gemv {
 constexpr int MAX_M = 8;
 int run(int dtype, const void* x, int64_t lda, const void* const w[3], const int64_t nrows[3], bool swiglu, void* y,
         int64_t ldy, int64_t m, int64_t n, int64_t k, const void* residual, const float* ssq_in, int ssq_parts,
-        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st, const L2Prefetch* pf = nullptr);
+        float ssq_inv_k, float ssq_eps, float* ssq_out, cudaStream_t st);
 }  // namespace gemv
 
 }  // namespace tk
