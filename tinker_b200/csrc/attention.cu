@@ -236,20 +236,23 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       constexpr uint32_t idesc_o = make_idesc_f16(Dx::umma_fmt, BQ, D, 0, 1);
       const uint32_t q_a = smem_u32(smem + S::Q_OFF), q_b = q_a + S::Q_BYTES;
       const uint32_t p_a = smem_u32(smem + S::P_OFF), p_b = p_a + S::P_BYTES;
-      auto issue_s = [&](uint32_t q_base, uint32_t k_base, uint32_t t_s) {
+      // Descriptors are built once per operand base; each K=16 step adds its byte offset / 16 to the
+      // start-address field (bases and offsets stay below 256 KB, so the 14-bit field never carries).
+      // This thread shares its scheduler with two busy softmax warps, so its instruction count per
+      // MMA decides how soon the next S is issued.
+      auto issue_s = [&](uint64_t q_desc, uint64_t k_desc, uint32_t t_s) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          umma_f16_ss(t_s, make_sw128_desc(q_base + off, 0, 1024), make_sw128_desc(k_base + off, 0, 1024), idesc_s,
-                      kk != 0);
+          const uint64_t off16 = static_cast<uint64_t>(((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4);
+          umma_f16_ss(t_s, q_desc + off16, k_desc + off16, idesc_s, kk != 0);
         }
       };
-      auto issue_pv = [&](uint32_t p_base, uint32_t v_base, uint32_t t_o, bool acc) {
+      auto issue_pv = [&](uint64_t p_desc, uint64_t v_desc, uint32_t t_o, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          umma_f16_ss(t_o, make_sw128_desc(p_base + aoff, 0, 1024),
-                      make_sw128_desc(v_base + kk * 16 * 128, BKV * 128, 1024), idesc_o, (acc || kk > 0) ? 1u : 0u);
+          const uint64_t aoff16 = static_cast<uint64_t>(((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4);
+          umma_f16_ss(t_o, p_desc + aoff16, v_desc + static_cast<uint64_t>(kk * 16 * 128 / 16), idesc_o,
+                      (acc || kk > 0) ? 1u : 0u);
         }
       };
       // K_j is ring item 2j, V_j item 2j + 1
@@ -258,7 +261,10 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         const int i = 2 * j;
         return mbar_wait(bars + B_FULL + i % NS, (i / NS) & 1);
       };
-      auto slot_addr = [&](int i) { return smem_u32(ring + (i % NS) * S::T_BYTES); };
+      auto k_desc = [&](int i) { return make_sw128_desc(smem_u32(ring + (i % NS) * S::T_BYTES), 0, 1024); };
+      auto v_desc = [&](int i) { return make_sw128_desc(smem_u32(ring + (i % NS) * S::T_BYTES), BKV * 128, 1024); };
+      const uint64_t qd_a = make_sw128_desc(q_a, 0, 1024), qd_b = make_sw128_desc(q_b, 0, 1024);
+      const uint64_t pd_a = make_sw128_desc(p_a, 0, 1024), pd_b = make_sw128_desc(p_b, 0, 1024);
       const uint32_t t_sa = tmem_base, t_sb = tmem_base + 128;
       const uint32_t t_oa = tmem_base + 256, t_ob = tmem_base + 256 + D;
 
@@ -267,10 +273,10 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
       bool ok = mbar_wait(bars + (ROPE ? B_Q_READY : B_Q_FULL), 0) && wait_k(0);
       if (ok) {
         tc_fence_after();
-        issue_s(q_a, slot_addr(0), t_sa);
+        issue_s(qd_a, k_desc(0), t_sa);
         umma_commit(bars + B_S_FULL + 0);
         if (has_b) {
-          issue_s(q_b, slot_addr(0), t_sb);
+          issue_s(qd_b, k_desc(0), t_sb);
           umma_commit(bars + B_S_FULL + 1);
         }
         umma_commit(bars + B_EMPTY + 0);  // K_0 consumed
@@ -284,13 +290,13 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
           if (j + 1 < n_a) {
             if (!mbar_wait(bars + B_S_FREE + 0, j & 1)) break;
             tc_fence_after();
-            issue_s(q_a, slot_addr(iv + 1), t_sa);
+            issue_s(qd_a, k_desc(iv + 1), t_sa);
             umma_commit(bars + B_S_FULL + 0);
           }
           if (has_b) {
             if (!mbar_wait(bars + B_S_FREE + 1, j & 1)) break;
             tc_fence_after();
-            issue_s(q_b, slot_addr(iv + 1), t_sb);
+            issue_s(qd_b, k_desc(iv + 1), t_sb);
             umma_commit(bars + B_S_FULL + 1);
           }
           umma_commit(bars + B_EMPTY + (iv + 1) % NS);  // K_{j+1} consumed
@@ -299,13 +305,13 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         if (j < n_a) {
           if (!mbar_wait(bars + B_P_FULL + 0, j & 1)) break;
           tc_fence_after();
-          issue_pv(p_a, slot_addr(iv), t_oa, j > 0);
+          issue_pv(pd_a, v_desc(iv), t_oa, j > 0);
           umma_commit(bars + B_PV_DONE + 0);
         }
         if (has_b) {
           if (!mbar_wait(bars + B_P_FULL + 1, j & 1)) break;
           tc_fence_after();
-          issue_pv(p_b, slot_addr(iv), t_ob, j > 0);
+          issue_pv(pd_b, v_desc(iv), t_ob, j > 0);
           umma_commit(bars + B_PV_DONE + 1);
         }
         umma_commit(bars + B_EMPTY + iv % NS);  // V_j consumed
