@@ -35,15 +35,24 @@ namespace attn {
 
 constexpr int BQ = 128;   // query rows per softmax warpgroup (one tcgen05 M=128 tile)
 constexpr int BKV = 128;  // keys per K/V tile
-constexpr int SOFTMAX_THREADS = 256;  // warps 0-3: query tile a, warps 4-7: query tile b
-constexpr int TMA_WARP = 8;
-constexpr int MMA_WARP = 9;
-constexpr int ROPE_WARP0 = 10;       // warps 10-11 rotate the K tiles (two rows per thread)
+// Warp roles. head_dim 64 runs four softmax warpgroups, two per query tile, each on one half of
+// the key columns of its rows (warps 0-3: tile a, columns 0-63; 4-7: tile b, 0-63; 8-11: tile a,
+// 64-127; 12-15: tile b, 64-127): the exponentials of a step are latency-bound with two warps per
+// scheduler, and four hide it better. head_dim 128 has no shared memory left for the halves'
+// exchange buffer and runs two (warps 0-3: tile a, 4-7: tile b, whole rows).
+template <int D>
+struct Roles {
+  static constexpr bool SPLIT = D == 64;
+  static constexpr int SOFTMAX_WARPS = SPLIT ? 16 : 8;
+  static constexpr int SOFTMAX_THREADS = SOFTMAX_WARPS * 32;
+  static constexpr int TMA_WARP = SOFTMAX_WARPS;
+  static constexpr int MMA_WARP = SOFTMAX_WARPS + 1;
+  static constexpr int ROPE_WARP0 = SOFTMAX_WARPS + 2;  // two warps rotate the K tiles (two rows per thread)
+  static constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;
+};
 constexpr int ROPE_K_THREADS = 64;
 constexpr float LAZY_RESCALE_LOG2 = 8.0f;  // move the running max only when it grows by more than 2^8
 
-// Three warpgroups in both variants (without RoPE, warps 10-11 only take part in set-up).
-__host__ __device__ constexpr int threads_for(bool) { return 384; }
 
 template <int D>
 struct Smem {
@@ -56,7 +65,10 @@ struct Smem {
   static constexpr int P_OFF = RING_OFF + STAGES * T_BYTES;  // P_a, P_b
   static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
   static constexpr int NUM_BARS = 24;
-  static constexpr int TOTAL = 1024 + BAR_OFF + NUM_BARS * 8 + 16;
+  // head_dim 64: the softmax halves' per-row partial maxima (and at the end their sums),
+  // [tile][step parity][half][row] fp32
+  static constexpr int RED_SPLIT_OFF = BAR_OFF + NUM_BARS * 8 + 16;
+  static constexpr int TOTAL = 1024 + RED_SPLIT_OFF + (Roles<D>::SPLIT ? 2 * 2 * 2 * BQ * 4 : 0);
   // single-tile CTAs (no query tile b): the per-row partial max and sum of the two column
   // halves, [4][128] fp32, in tile b's Q slot
   static constexpr int RED_OFF = Q_OFF + Q_BYTES;
@@ -151,10 +163,11 @@ __device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, int64_t p
 }
 
 template <int DT, int D, bool ROPE>
-__global__ void __launch_bounds__(threads_for(ROPE), 1)
+__global__ void __launch_bounds__(Roles<D>::THREADS, 1)
     rope_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const Params p) {
   using S = Smem<D>;
+  using R = Roles<D>;
   using Dx = Dt<DT>;
   constexpr int NS = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
 
   if (tid == 0) {
     mbar_init(bars + B_Q_FULL, 1);
-    mbar_init(bars + B_Q_READY, SOFTMAX_THREADS);
+    mbar_init(bars + B_Q_READY, R::SOFTMAX_THREADS);
     for (int i = 0; i < NS; ++i) {
       mbar_init(bars + B_FULL + i, 1);
       mbar_init(bars + B_EMPTY + i, 1);
@@ -189,13 +202,13 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bars + B_K_READY + i, ROPE_K_THREADS);
       mbar_init(bars + B_S_FULL + i, 1);
-      mbar_init(bars + B_P_FULL + i, single ? 256 : 128);
+      mbar_init(bars + B_P_FULL + i, R::SPLIT || single ? 256 : 128);
       mbar_init(bars + B_PV_DONE + i, 1);
-      mbar_init(bars + B_S_FREE + i, 128);
+      mbar_init(bars + B_S_FREE + i, R::SPLIT ? 256 : 128);
     }
     fence_mbar_init();
   }
-  if (warp == MMA_WARP) {
+  if (warp == R::MMA_WARP) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == TMA_WARP) {
+  if (warp == R::TMA_WARP) {
     // ---------------- TMA producer: Q_a|Q_b, then K_0, V_0, K_1, V_1, ... ----------------
     if (lane == 0) {
       pdl_launch_dependents();
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
           tma_load_3d(dst + cb * 128 * 128, m, bars + B_FULL + slot, kvh * D + cb * 64, (i >> 1) * BKV, b);
       }
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == R::MMA_WARP) {
     // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(Dx::umma_fmt, BQ, BKV, 0, 0);
@@ -317,11 +330,11 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         umma_commit(bars + B_EMPTY + iv % NS);  // V_j consumed
       }
     }
-  } else if (warp >= ROPE_WARP0) {
+  } else if (warp >= R::ROPE_WARP0) {
     // ---------------- RoPE of the K tiles (rows t and t + 64) ----------------
     if constexpr (ROPE) {
       pdl_wait();  // the tables may have been written by the previous kernel
-      const int t = tid - ROPE_WARP0 * 32;
+      const int t = tid - R::ROPE_WARP0 * 32;
       for (int j = 0; j < n_kv; ++j) {
         const int i = 2 * j;
         uint8_t* kt = ring + (i % NS) * S::T_BYTES;
@@ -350,7 +363,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         mbar_arrive(bars + B_K_READY + (j & 1));
       }
     }
-  } else if (warp < 8 && single) {
+  } else if (!R::SPLIT && warp < 8 && single) {
     // ---------------- one key tile: warpgroup h takes key columns [64 h, 64 h + 64) of row r ----------------
     const int h2 = warp >> 2;
     const int r = tid & 127;
@@ -390,7 +403,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
     for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
     red[h2 * BQ + r] = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-    named_sync(1, SOFTMAX_THREADS);
+    named_sync(1, R::SOFTMAX_THREADS);
     // column 0 is never masked, so the row maximum is finite
     const float neg_m = -fmaxf(red[r], red[BQ + r]) * p.scale_log2;
     const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), negm2 = pack_f32x2(neg_m, neg_m);
@@ -422,7 +435,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
 #pragma unroll
     for (int i = 0; i < 4; ++i) unpack_f32x2(rs2[i], rp[2 * i], rp[2 * i + 1]);
     red[(2 + h2) * BQ + r] = ((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7]));
-    named_sync(1, SOFTMAX_THREADS);
+    named_sync(1, R::SOFTMAX_THREADS);
     const float inv_l = 1.0f / (red[2 * BQ + r] + red[3 * BQ + r]);
     // O / l: warpgroup h2 writes output columns [h2 D/2, h2 D/2 + D/2) of row r
     if (ok && mbar_wait(bars + B_PV_DONE + 0, 0)) {
@@ -448,7 +461,145 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
         }
       }
     }
-  } else if (warp < 8) {
+  } else if (R::SPLIT && warp < R::SOFTMAX_WARPS) {
+    // ---------------- softmax, head_dim 64: tile x, key columns [64 hh, 64 hh + 64) of row r ----------------
+    const int x = (warp >> 2) & 1;
+    const int hh = warp >> 3;
+    const int r = tid & 127;
+    const int qt = 2 * blk + x;
+    const int q_row = qt * BQ + r;
+    const bool active = x == 0 || has_b;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem_base + x * 128 + hh * 64;
+    const uint32_t t_o = tmem_base + 256 + x * D + hh * (D / 2);
+    uint8_t* sq = smem + S::Q_OFF + x * S::Q_BYTES;
+    uint8_t* sp = smem + S::P_OFF + x * S::P_BYTES + hh * (128 * 128);  // this half's 64-key atom of P
+    float* red = reinterpret_cast<float*>(smem + S::RED_SPLIT_OFF) + x * (2 * 2 * BQ);
+    bool ok = true;
+    if constexpr (ROPE) {
+      const int64_t qpos = static_cast<int64_t>(p.start_pos) + q_row;
+      const bool valid = active && hh == 0 && q_row < p.seq;
+      float c[32], sn[32];
+      pdl_wait();  // the tables may have been written by the previous kernel
+      if (valid) rope_load_block(p, qpos, 0, D / 2, c, sn);  // in flight while the Q tile lands
+      ok = mbar_wait(bars + B_Q_FULL, 0);
+      if (ok && valid) rope_apply_block<DT>(sq, r, 0, c, sn);
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(bars + B_Q_READY);
+    const int n_x = x == 0 ? n_a : n_a + 1;
+    float m_run = -INFINITY, l_run = 0.f;
+    // every step reaches the halves' barrier, also after a timed-out wait (the other half waits there)
+    for (int j = 0; active && j < n_x; ++j) {
+      if (ok) ok = mbar_wait(bars + B_S_FULL + x, j & 1);
+      tc_fence_after();
+      float sv[64];
+      tmem_load64(t_s + lane_off, sv);
+      // S is in registers: the MMA may write the next tile's scores over it
+      tc_fence_before();
+      mbar_arrive(bars + B_S_FREE + x);
+      if (j == qt) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (j * BKV + hh * 64 + c > q_row) sv[c] = -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+      // the row maximum of this step: both halves' partial maxima, double-buffered by step parity
+      // (a half overwrites a slot only after the barrier of the next step, which its partner
+      // passes only once it has read the slot)
+      float* rj = red + (j & 1) * (2 * BQ);
+      rj[hh * BQ + r] = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      named_sync(1 + x, 256);
+      const float mx = fmaxf(rj[r], rj[BQ + r]) * p.scale_log2;
+      // lazy rescale: keep the old maximum unless this tile exceeds it by more than 2^8 (both
+      // halves see the same maxima, so they take the same decision)
+      float m_use = m_run, alpha = 1.f;
+      if (mx > m_run + LAZY_RESCALE_LOG2) {
+        m_use = mx;
+        alpha = exp2_approx(m_run - mx);
+      }
+      const float neg_m = -m_use;
+      const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), negm2 = pack_f32x2(neg_m, neg_m);
+      uint64_t rs2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        const uint64_t e = fma_f32x2(pack_f32x2(sv[c], sv[c + 1]), scale2, negm2);
+        float e0, e1;
+        unpack_f32x2(e, e0, e1);
+        sv[c] = exp2_approx(e0);
+        sv[c + 1] = exp2_approx(e1);
+        rs2[(c >> 1) & 3] = add_f32x2(rs2[(c >> 1) & 3], pack_f32x2(sv[c], sv[c + 1]));
+      }
+      float rp[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) unpack_f32x2(rs2[i], rp[2 * i], rp[2 * i + 1]);
+      l_run = l_run * alpha + (((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7])));
+      m_run = m_use;
+      if (j > 0 && ok) {
+        // P and the O accumulator are still in use by the previous P.V
+        ok = mbar_wait(bars + B_PV_DONE + x, (j - 1) & 1);
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(sp + r * 128 + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int c = 0; c < D / 2; c += 32) {
+          float o[32];
+          tmem_load32(t_o + lane_off + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_o + lane_off + c, o);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bars + B_P_FULL + x);
+    }
+    if (active) {
+      // the row sum: both halves' partial sums, through the parity slot no step still reads
+      float* rs_buf = red + (n_x & 1) * (2 * BQ);
+      rs_buf[hh * BQ + r] = l_run;
+      named_sync(1 + x, 256);
+      const float inv_l = 1.0f / (rs_buf[r] + rs_buf[BQ + r]);
+      if (ok && mbar_wait(bars + B_PV_DONE + x, (n_x - 1) & 1)) {
+        tc_fence_after();
+        using T = typename Dx::T;
+        T* dst = reinterpret_cast<T*>(p.out) +
+                 (static_cast<int64_t>(b) * p.seq + q_row) * p.out_tok_stride + static_cast<int64_t>(h) * D + hh * (D / 2);
+#pragma unroll
+        for (int c = 0; c < D / 2; c += 32) {
+          float o[32];
+          tmem_load32(t_o + lane_off + c, o);
+          if (q_row < p.seq) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                typename Dx::T2 hv = Dx::pack(o[q * 8 + 2 * i] * inv_l, o[q * 8 + 2 * i + 1] * inv_l);
+                w[i] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+              reinterpret_cast<uint4*>(dst + c)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  } else if (!R::SPLIT && warp < 8) {
     // ---------------- softmax / correction / output: warpgroup x, thread = query row ----------------
     const int x = warp >> 2;
     const int r = tid & 127;
@@ -590,7 +741,7 @@ __global__ void __launch_bounds__(threads_for(ROPE), 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == MMA_WARP) {
+  if (warp == R::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
@@ -615,7 +766,7 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
       return rc;
     configured[dev.device] = true;
   }
-  return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(threads_for(ROPE)), S::TOTAL, st, 1,
+  return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(Roles<D>::THREADS), S::TOTAL, st, 1,
                        ROPE ? "rope_attention_kernel" : "causal_attention_kernel", tq, tk_, tv, p);
 }
 
