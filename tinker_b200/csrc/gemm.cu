@@ -1070,14 +1070,18 @@ static int max_active_clusters(int bn, int split, int smem) {
   return n;
 }
 
-// Cost model fitted to timestamped runs of both kernels at M = 128 on B200 (µs):
-// ~1.8 of set-up and first-load latency, the CTA's k-slice of activations plus
-// weights at ~100 GB/s per SM (shared by the CTAs an SM holds), and for split > 1
-// a DSMEM reduction of ~0.8 + (partial bytes sent) / 25 GB/s; the owner epilogue
-// grows with BN. Split-K plans must fit in one wave of co-resident clusters,
-// costed with <= 4-stage rings (two CTAs per SM); a plan of one CTA per SM then
-// gets a deep ring (below). Splits stay <= 4 and BN <= 64 (beyond that the
-// reduction and cluster barriers dominate).
+// Cost model (µs) for a CTA's critical path at M <= a few hundred rows on B200, fitted to A/B timings
+// of the 268M decoder's projections at 128 rows inside its CUDA graph: ~1.8 of set-up and first
+// load; ~1.0 per round trip of the ring (at these sizes a k-block's TMA round trip from L2 costs
+// more than its transfer, so a CTA's stream takes ceil(k-blocks / stages) round trips) plus the
+// bytes at ~200 GB/s per SM; for split > 1 a DSMEM reduction of ~0.5 + 0.35 per extra CTA of
+// the cluster + (partial bytes sent) / 25 GB/s; an owner epilogue that grows with BN. Plans of one
+// wave with one CTA per SM get a deep ring (8 stages, split-K: as many as the CTA's k-blocks);
+// other split-K plans <= 4 stages (two CTAs per SM) and must fit in one wave of co-resident
+// clusters. Splits stay <= 4 and BN <= 64; splits are tried from the largest down, and a later
+// candidate must be 3 % cheaper to replace an earlier one.
+// Measured against the earlier bandwidth-only model: o_proj at 128 rows moves from split 4 to
+// split 2 (one round trip either way, half the exchange partners): 564 -> 548 us per forward.
 template <int DT, int EPI>
 static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sms, int64_t constraint,
                               size_t smem_cap) {
@@ -1089,46 +1093,40 @@ static SmallPlan plan_small_m(int64_t m_tiles, int64_t n_out, int num_kb, int sm
     const int64_t per_tile_n = swiglu ? bn / 2 : bn;
     if (!swiglu && constraint % bn != 0) continue;
     const int64_t n_tiles = (n_out + per_tile_n - 1) / per_tile_n;
-    for (int split = 1; split <= 4; ++split) {
-      if (split > num_kb) break;
-      const int64_t ctas = m_tiles * n_tiles * split;
-      const double kb_per_cta = double(num_kb) / split;
+    const int64_t tiles = m_tiles * n_tiles;
+    for (int split = 4; split >= 1; --split) {
+      if (split > num_kb) continue;
+      const int64_t ctas = tiles * split;
+      const int kb = (num_kb + split - 1) / split;  // k-blocks of the busiest CTA
+      const bool one_wave = ctas <= sms;
       int stages = 0;
       if (split > 1) {
-        const int want = std::min<int>(4, int(std::ceil(kb_per_cta)));
+        const int want = std::min(4, kb);
         for (int s = want; s >= 2; --s)
           if (static_cast<size_t>(splitk_smem(bn, split, s)) <= smem_cap) { stages = s; break; }
         if (stages < std::min(want, 3)) continue;
-        const int clusters = max_active_clusters<DT, EPI>(bn, split, splitk_smem(bn, split, stages));
-        if (m_tiles * n_tiles > clusters) continue;  // the split kernel must run in one wave
+        if (tiles > max_active_clusters<DT, EPI>(bn, split, splitk_smem(bn, split, stages)))
+          continue;  // the split kernel must run in one wave
+        if (one_wave && kb > stages) {
+          const int deep = std::min(SplitSmem<32>::MAX_STAGES, kb);
+          const int smem = splitk_smem(bn, split, deep);
+          if (static_cast<size_t>(smem) <= smem_cap && tiles <= max_active_clusters<DT, EPI>(bn, split, smem))
+            stages = deep;
+        }
+      } else {
+        stages = one_wave && kb > 4 ? DEEP_STAGES : 4;
       }
-      const double load = kb_per_cta * (BM * BK * 2 + bn * BK * 2);
+      const int trips = (kb + stages - 1) / stages;
+      const double load = double(kb) * (BM * BK * 2 + bn * BK * 2);
       const double red = split > 1 ? 128.0 * bn * 4 * (split - 1) / split : 0.0;
       const double per_sm = split > 1 ? std::max(1.0, double(ctas) / sms) : double((ctas + sms - 1) / sms);
-      const double cost = 1.8 + per_sm * load / 100e3 + (split > 1 ? 0.8 + red / 25e3 : 0.0) + 0.25 * bn / 32;
+      const double cost = 1.8 + per_sm * (trips * 1.0 + load / 200e3) +
+                          (split > 1 ? 0.5 + 0.35 * (split - 1) + red / 25e3 : 0.0) + 0.25 * bn / 32;
       if (cost < best_cost * 0.97) {
         best_cost = cost;
         best.bn = bn;
         best.split = split;
         best.stages = stages;
-      }
-    }
-  }
-  // One wave with one CTA per SM: a deep ring. At a few hundred rows every k-block's TMA
-  // round trip (L2 latency under load, ~1.5 us) costs more than its transfer, so the CTA's
-  // stream runs in ceil(k-blocks / stages) round trips; 8 stages halve them against 4 (a
-  // CTA then fills its SM's shared memory, so the next kernel's CTA no longer starts beside it).
-  if (best.bn) {
-    const int64_t tiles = m_tiles * ((n_out + (swiglu ? best.bn / 2 : best.bn) - 1) / (swiglu ? best.bn / 2 : best.bn));
-    const int kb_per_cta = (num_kb + best.split - 1) / best.split;
-    if (tiles * best.split <= sms && kb_per_cta > best.stages) {
-      const int deep = std::min(SplitSmem<32>::MAX_STAGES, kb_per_cta);
-      if (best.split == 1) {
-        best.stages = DEEP_STAGES;
-      } else if (static_cast<size_t>(splitk_smem(best.bn, best.split, deep)) <= smem_cap &&
-                 max_active_clusters<DT, EPI>(best.bn, best.split, splitk_smem(best.bn, best.split, deep)) >=
-                     m_tiles * ((n_out + (swiglu ? best.bn / 2 : best.bn) - 1) / (swiglu ? best.bn / 2 : best.bn))) {
-        best.stages = deep;
       }
     }
   }
