@@ -1,7 +1,7 @@
 """Standalone kernel sweeps and the ~1B decoder, each against the reference's eager torch path
 on the same GPU.
 
-    python -m tinker_b200.sweep [--only rmsnorm,ffn,attention,model1b] [--dtypes fp16,bf16]
+    python bench_sweep.py [--only rmsnorm,ffn,attention,model1b] [--dtypes fp16,bf16]
 
 One JSON line per case on stdout. The cases are the standalone configurations the reference
 benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of
