@@ -262,3 +262,26 @@ def test_folded_norm_arguments_rejected():
     rc = _lib.lib().tk_gate_up_swiglu_ex(x.data_ptr(), 256, w.data_ptr(), w.data_ptr(), h.data_ptr(), 128, 256, 64, e,
                                          0, _lib.stream_ptr(x.device))
     assert rc == _lib.TK_ERR_INVALID
+
+
+@pytest.mark.parametrize("m, n, k", [(128, 1024, 1024), (128, 1024, 2816), (300, 896, 896), (4, 1024, 1024)])
+def test_l2_prefetch_hints_change_no_result(m, n, k):
+    """tk_epilogue.l2_prefetch only pulls ranges into L2: the products with hints (aligned and
+    unaligned ranges, more ranges than slots, an empty tensor, the output itself) are bitwise those
+    without, for the split-K, plain and weight-streaming kernels."""
+    require_b200()
+    from tinker_b200.kernels.gemm import gate_up_swiglu, linear
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    x = torch.randn(m, k, device="cuda", generator=g).half()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).half()
+    r = torch.randn(m, n, device="cuda", generator=g).half()
+    other = torch.randn(3 << 20, device="cuda", generator=g).half()
+    hints = (other[1:], w, other[5:1000], torch.empty(0, device="cuda"), r, x, other, w[:, 3:].contiguous(), x[1:])
+    y0 = linear(x, w, residual=r)
+    y1 = linear(x, w, residual=r, l2_prefetch=hints)
+    h0 = gate_up_swiglu(x, w, w)
+    h1 = gate_up_swiglu(x, w, w, l2_prefetch=hints[:3])
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    assert torch.equal(h0, h1)
+    assert rel_err(np32(y1), _ref(x, [w], r)) <= TOL[torch.float16]
