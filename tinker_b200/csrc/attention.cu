@@ -72,7 +72,8 @@ struct Smem {
   // single-tile CTAs (no query tile b): the per-row partial max and sum of the two column
   // halves, [4][128] fp32, in tile b's Q slot
   static constexpr int RED_OFF = Q_OFF + Q_BYTES;
-  // S_a: 0-127, S_b: 128-255, O_a: 256.., O_b: 256 + head_dim..
+  // S_a: 0-127, S_b: 128-255, O_a: 256.., O_b: 256 + head_dim..; head_dim 64 keeps P in the last
+  // 128 columns (P_a: 384-447, P_b: 448-511, 16-bit pairs) as the A operand of P.V
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
@@ -260,12 +261,17 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
           umma_f16_ss(t_s, q_desc + off16, k_desc + off16, idesc_s, kk != 0);
         }
       };
-      auto issue_pv = [&](uint64_t p_desc, uint64_t v_desc, uint32_t t_o, bool acc) {
+      auto issue_pv = [&](uint64_t p_desc, uint32_t p_tmem, uint64_t v_desc, uint32_t t_o, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t aoff16 = static_cast<uint64_t>(((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4);
-          umma_f16_ss(t_o, p_desc + aoff16, v_desc + static_cast<uint64_t>(kk * 16 * 128 / 16), idesc_o,
-                      (acc || kk > 0) ? 1u : 0u);
+          if constexpr (R::SPLIT) {  // P in tensor memory: 8 columns per K=16 step
+            umma_f16_ts(t_o, p_tmem + kk * 8, v_desc + static_cast<uint64_t>(kk * 16 * 128 / 16), idesc_o,
+                        (acc || kk > 0) ? 1u : 0u);
+          } else {
+            const uint64_t aoff16 = static_cast<uint64_t>(((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4);
+            umma_f16_ss(t_o, p_desc + aoff16, v_desc + static_cast<uint64_t>(kk * 16 * 128 / 16), idesc_o,
+                        (acc || kk > 0) ? 1u : 0u);
+          }
         }
       };
       // K_j is ring item 2j, V_j item 2j + 1
@@ -318,13 +324,13 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
         if (j < n_a) {
           if (!mbar_wait(bars + B_P_FULL + 0, j & 1)) break;
           tc_fence_after();
-          issue_pv(pd_a, v_desc(iv), t_oa, j > 0);
+          issue_pv(pd_a, tmem_base + 384, v_desc(iv), t_oa, j > 0);
           umma_commit(bars + B_PV_DONE + 0);
         }
         if (has_b) {
           if (!mbar_wait(bars + B_P_FULL + 1, j & 1)) break;
           tc_fence_after();
-          issue_pv(pd_b, v_desc(iv), t_ob, j > 0);
+          issue_pv(pd_b, tmem_base + 448, v_desc(iv), t_ob, j > 0);
           umma_commit(bars + B_PV_DONE + 1);
         }
         umma_commit(bars + B_EMPTY + iv % NS);  // V_j consumed
@@ -473,7 +479,7 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
     const uint32_t t_s = tmem_base + x * 128 + hh * 64;
     const uint32_t t_o = tmem_base + 256 + x * D + hh * (D / 2);
     uint8_t* sq = smem + S::Q_OFF + x * S::Q_BYTES;
-    uint8_t* sp = smem + S::P_OFF + x * S::P_BYTES + hh * (128 * 128);  // this half's 64-key atom of P
+    const uint32_t t_p = tmem_base + 384 + x * 64 + hh * 32;  // this half's 64 keys of P, packed in pairs
     float* red = reinterpret_cast<float*>(smem + S::RED_SPLIT_OFF) + x * (2 * 2 * BQ);
     bool ok = true;
     if constexpr (ROPE) {
@@ -545,15 +551,14 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
         ok = mbar_wait(bars + B_PV_DONE + x, (j - 1) & 1);
         tc_fence_after();
       }
+      {
+        uint32_t w[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          typename Dx::T2 hv = Dx::pack(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
+        for (int i = 0; i < 32; ++i) {
+          typename Dx::T2 hv = Dx::pack(sv[2 * i], sv[2 * i + 1]);
           w[i] = *reinterpret_cast<uint32_t*>(&hv);
         }
-        *reinterpret_cast<uint4*>(sp + r * 128 + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st32u(t_p + lane_off, w);  // waits for its own completion
       }
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
@@ -565,7 +570,6 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
           tmem_st32(t_o + lane_off + c, o);
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bars + B_P_FULL + x);
     }
