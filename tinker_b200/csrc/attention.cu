@@ -182,9 +182,11 @@ __global__ void __launch_bounds__(Roles<D>::THREADS, 1)
   const int lane = tid & 31;
   // CTA = query tiles a = 2*blk and b = 2*blk + 1 of one (batch, head); heaviest pairs first
   const int n_pairs = (p.n_qtiles + 1) >> 1;
-  const int blk = n_pairs - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  // the pair index is the grid's slowest dimension, so CTAs start heaviest pair first across all
+  // heads and sequences (longest-first list scheduling over the SMs)
+  const int blk = n_pairs - 1 - static_cast<int>(blockIdx.z);
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
   const int kvh = h / p.groups;
   const bool has_b = 2 * blk + 1 < p.n_qtiles;
   const int n_a = 2 * blk + 1;             // key tiles of query tile a (causal)
@@ -770,7 +772,7 @@ int launch(const void* q, int64_t qs, const void* k, int64_t ks, const void* v, 
       return rc;
     configured[dev.device] = true;
   }
-  return launch_kernel(kern, dim3((p.n_qtiles + 1) / 2, p.num_heads, p.batch), dim3(Roles<D>::THREADS), S::TOTAL, st, 1,
+  return launch_kernel(kern, dim3(p.num_heads, p.batch, (p.n_qtiles + 1) / 2), dim3(Roles<D>::THREADS), S::TOTAL, st, 1,
                        ROPE ? "rope_attention_kernel" : "causal_attention_kernel", tq, tk_, tv, p);
 }
 
@@ -842,7 +844,8 @@ int prepare(const char* what, const void* q, int64_t q_tok_stride, const void* k
     return fail_invalid("attention: token stride smaller than heads * head_dim");
   if (q_tok_stride % 8 || k_tok_stride % 8 || v_tok_stride % 8 || out_tok_stride % 8)
     return fail_invalid("attention: token strides must be multiples of 8 elements");
-  if (num_heads > 65535 || batch > 65535) return fail_invalid("attention: too many heads or batches");
+  if (num_heads > 65535 || batch > 65535 || (int64_t(seq) + 2 * BQ - 1) / (2 * BQ) > 65535)
+    return fail_invalid("attention: too many heads, batches or query tiles");
   if (batch == 0 || seq == 0) {  // empty tensors may carry NULL data pointers
     *empty = true;
     return TK_OK;
