@@ -255,3 +255,27 @@ def test_reference_import_paths_resolve_to_this_package():
     from tinker.optimize import benchmark_model as bm
     assert tinker.optimize is tinker_b200.optimize and pm is tinker_b200.patch_model
     assert fr is fused_rmsnorm and TA is TinKerAttention and TS is TinKerSwiGLU and bm is tinker_b200.benchmark_model
+
+
+def test_prefetch_chain_links_blocks_in_order_and_caps_the_head():
+    """``link_ahead`` points every fused block at the next one and the last at the LM head;
+    ``_ahead_weights`` names the next block's folded q|k|v weights once they exist, the head
+    weight unless it is larger than the cap (a tied 150k-token table would not stay in L2)."""
+    from tinker_b200 import fusion
+    m = build_model(TINY.with_(num_layers=3))
+    tinker_b200.patch_model(m)
+    for blk in m.layers:  # what fuse_decoder_blocks records once a block passed its checks
+        blk._tinker_block_parts = fusion._block_parts(blk)
+    assert fusion.link_ahead(m) == 3
+    b0, b1, b2 = m.layers
+    assert b0._tinker_ahead() is b1 and b1._tinker_ahead() is b2 and b2._tinker_ahead() is m.output
+    assert fusion._ahead_weights(b0) == ()  # the next block has not folded its weights yet
+    folded = tuple(torch.zeros(2, 2) for _ in range(5))
+    b1._tinker_folded = (None, folded)
+    assert fusion._ahead_weights(b0) == folded[:3]
+    assert fusion._ahead_weights(b2) == (m.output.weight,)
+    big = nn.Linear(8, (fusion._AHEAD_MAX_BYTES // 32) + 1, bias=False)  # just above the cap in fp32
+    m.output = big
+    fusion.link_ahead(m)
+    assert fusion._ahead_weights(b2) == ()
+    assert "_tinker_ahead" not in dict(m.named_modules())  # plain attributes, not submodules
