@@ -1,26 +1,28 @@
 // Fused RoPE + GQA/MQA/MHA causal attention on tcgen05 tensor cores.
 //
 // One CTA computes a PAIR of 128-row query tiles (a = 2 * blk, b = 2 * blk + 1) of one
-// (batch, query head); the heaviest pairs are scheduled first. 384 threads, five roles
-// working through mbarriers:
-//   * warp 8 (TMA): loads the two raw Q tiles once, then streams K_0, V_0, K_1, V_1, ...
+// (batch, query head). The pair index is the grid's slowest dimension, so the heaviest pairs of
+// every head and sequence start first. Roles working through mbarriers (warp numbers for head_dim
+// 64; head_dim 128 has eight softmax warps and the other roles start at warp 8):
+//   * warp 16 (TMA): loads the two raw Q tiles once, then streams K_0, V_0, K_1, V_1, ...
 //     of KV head h / groups through a ring of 4 (head_dim 64) or 3 (head_dim 128) slots,
 //     straight from the [batch, seq, heads, head_dim] projection layout (token strides
 //     are free, so q/k/v may be column slices of one fused q|k|v output) into
 //     128-byte-swizzled shared memory. Tile b needs one key tile more than tile a.
-//   * warps 10-11 (RoPE, drop-in entry only): rotate the interleaved pairs of every K row
+//   * warps 18-19 (RoPE, drop-in entry only): rotate the interleaved pairs of every K row
 //     in place in shared memory, in fp32, rounding back to the input dtype as the
 //     reference does before its attention kernel (tinker/kernels/fused_attention.py
 //     :203-214, :53-69). The softmax warps rotate their Q tile the same way, once.
-//   * warp 9 (MMA, one thread): S_a = Q_a K_j^T and S_b = Q_b K_j^T as tcgen05.mma
-//     (M=128, N=128, K=head_dim) into two TMEM S buffers, then O_a += P_a V_j and
-//     O_b += P_b V_j with V as an MN-major operand into two TMEM O accumulators.
-//   * warps 0-3 (tile a) and 4-7 (tile b), softmax, thread i owns query row i: read S
-//     with tcgen05.ld, mask the diagonal tile, run the online softmax with exp2, write P
-//     (rounded to the input dtype) to shared memory and rescale the running O in TMEM.
-//     The running maximum is only moved when a tile raises it by more than 2^8 (a lazy
-//     rescale): P stays below 256 and O is rescaled on few tiles. The final O / l is
-//     written by the same threads.
+//   * warp 17 (MMA, one thread): S_a = Q_a K_j^T and S_b = Q_b K_j^T as tcgen05.mma
+//     (M=128, N=128, K=head_dim) into two TMEM S buffers - the next S of a tile as soon as
+//     its softmax has read the current one into registers - then O_a += P_a V_j and
+//     O_b += P_b V_j with V as an MN-major operand into two TMEM O accumulators, P read
+//     from TMEM at head_dim 64 and from shared memory at head_dim 128.
+//   * softmax warpgroups (see Roles), thread = query row: read S with tcgen05.ld, mask the
+//     diagonal tile, run the online softmax with exp2, write P (rounded to the input dtype)
+//     and rescale the running O in TMEM. The running maximum is only moved when a tile
+//     raises it by more than 2^8 (a lazy rescale): P stays below 256 and O is rescaled on
+//     few tiles. The final O / l is written by the same threads.
 // Causal tiles above the diagonal are skipped. The arithmetic follows _attention_kernel
 // (tinker/kernels/fused_attention.py:74-154): scale 1/sqrt(head_dim), running max / sum
 // in fp32, output divided by the sum.
@@ -37,8 +39,8 @@ constexpr int BQ = 128;   // query rows per softmax warpgroup (one tcgen05 M=128
 constexpr int BKV = 128;  // keys per K/V tile
 // Warp roles. head_dim 64 runs four softmax warpgroups, two per query tile, each on one half of
 // the key columns of its rows (warps 0-3: tile a, columns 0-63; 4-7: tile b, 0-63; 8-11: tile a,
-// 64-127; 12-15: tile b, 64-127): the exponentials of a step are latency-bound with two warps per
-// scheduler, and four hide it better. head_dim 128 has no shared memory left for the halves'
+// 64-127; 12-15: tile b, 64-127), exchanging the row maximum per step through shared memory; it
+// measured a few percent faster than two. head_dim 128 has no shared memory left for the
 // exchange buffer and runs two (warps 0-3: tile a, 4-7: tile b, whole rows).
 template <int D>
 struct Roles {
