@@ -55,16 +55,22 @@ __device__ __forceinline__ float row_scale(const Params& p, int row) {
 }
 
 // SWIGLU: column j needs gate row j and up row j (ROWS = 2 * CPW weight rows per warp).
-// CL: CTAs per cluster (WARPS * CPW * CL == 32 when ssq_out is used).
-template <int DT, int M, int CPW, bool SWIGLU, int CL>
+// KS: warps per column group, each on 1/KS of K (the partial sums meet in shared memory): a
+// long row (the down projection of a decode step) then takes fewer rounds of loads per lane.
+// CL: CTAs per cluster ((WARPS / KS) * CPW * CL == 32 when ssq_out is used).
+template <int DT, int M, int CPW, bool SWIGLU, int CL, int KS>
 __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
   using T = typename Dt<DT>::T;
   constexpr int ROWS = SWIGLU ? 2 * CPW : CPW;
+  constexpr int CWARPS = WARPS / KS;  // column groups per CTA
   __shared__ float ssq_s[WARPS][M];
   __shared__ float cta_ssq[M];
+  __shared__ float part[KS > 1 ? CWARPS : 1][KS > 1 ? ROWS : 1][KS > 1 ? M : 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int col0 = (blockIdx.x * WARPS + warp) * CPW;  // first output column of this warp
-  const int kc = p.k >> 3;                              // 16-byte chunks per row
+  const int kpart = warp / CWARPS;                                 // which 1/KS of K
+  const int col0 = (blockIdx.x * CWARPS + warp % CWARPS) * CPW;  // first output column of this warp
+  const int kc = p.k >> 3;                                        // 16-byte chunks per row
+  const int kbeg = kpart * kc / KS, kend = (kpart + 1) * kc / KS;
 
   // weight row pointers (null past the end)
   const T* wrow[ROWS];
@@ -87,7 +93,7 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
   // the weights do not depend on the previous kernel: start pulling them into L2
   for (int r = 0; r < ROWS; ++r)
     if (wrow[r])
-      for (int c = lane * 8; c < kc; c += 32 * 8) prefetch_l2(wrow[r] + static_cast<int64_t>(c) * 8);
+      for (int c = kbeg + lane * 8; c < kend; c += 32 * 8) prefetch_l2(wrow[r] + static_cast<int64_t>(c) * 8);
   pdl_wait();
 
   uint64_t acc[ROWS][M];
@@ -97,7 +103,7 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
     for (int m = 0; m < M; ++m) acc[r][m] = 0ull;
   const T* xb = reinterpret_cast<const T*>(p.x);
 #pragma unroll 4  // a 1024-wide row in one round of loads per lane
-  for (int c = lane; c < kc; c += 32) {
+  for (int c = kbeg + lane; c < kend; c += 32) {
     uint4 wv[ROWS];
 #pragma unroll
     for (int r = 0; r < ROWS; ++r)
@@ -135,6 +141,19 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       sum[r][m] = s;
     }
+  if constexpr (KS > 1) {  // the warps of the second half of K hand their sums to the first
+    if (kpart == 1 && lane == 0)
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) part[warp % CWARPS][r][m] = sum[r][m];
+    __syncthreads();
+    if (kpart == 0)
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) sum[r][m] += part[warp][r][m];
+  }
 
   // epilogue: lane (c * M + m) stores output column col0 + c of row m
   float sq[M];
@@ -145,7 +164,7 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const int col = col0 + c;
-      if (m >= p.m || col >= p.n) continue;
+      if (kpart != 0 || m >= p.m || col >= p.n) continue;  // one writer per column
       const float sc = row_scale(p, m);
       float v;
       if (SWIGLU) {
@@ -188,11 +207,11 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
   }
 }
 
-template <int DT, int M, int CPW, bool SWIGLU, int CL>
+template <int DT, int M, int CPW, bool SWIGLU, int CL, int KS = 1>
 int launch_m(const Params& p, cudaStream_t st) {
-  const int cols = WARPS * CPW;
+  const int cols = (WARPS / KS) * CPW;
   const int grid = ((p.n + cols - 1) / cols + CL - 1) / CL * CL;  // whole clusters
-  return launch_kernel(gemv_kernel<DT, M, CPW, SWIGLU, CL>, dim3(grid), dim3(THREADS), 0, st, CL, "gemv", p);
+  return launch_kernel(gemv_kernel<DT, M, CPW, SWIGLU, CL, KS>, dim3(grid), dim3(THREADS), 0, st, CL, "gemv", p);
 }
 
 template <int DT, int CPW, bool SWIGLU, int CL>
@@ -209,6 +228,9 @@ int launch_cpw(const Params& p, cudaStream_t st) {
 template <int DT>
 int launch_dt(const Params& p, bool swiglu, int cpw, cudaStream_t st) {
   if (swiglu) return cpw == 1 ? launch_cpw<DT, 1, true, 1>(p, st) : launch_cpw<DT, 2, true, 1>(p, st);
+  // one row against a long weight row (K >= 2048, e.g. the down projection of a decode step):
+  // two warps per column, each on half of K; 4 columns per CTA, 8 CTAs per 32-column chunk
+  if (p.ssq_out && p.m == 1 && p.k >= 2048) return launch_m<DT, 1, 1, false, 8, 2>(p, st);
   if (p.ssq_out) return launch_cpw<DT, 1, false, 4>(p, st);  // 8 columns per CTA, 4 CTAs per chunk
   if (cpw == 4) return launch_cpw<DT, 4, false, 1>(p, st);
   return cpw == 2 ? launch_cpw<DT, 2, false, 1>(p, st) : launch_cpw<DT, 1, false, 1>(p, st);
