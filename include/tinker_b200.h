@@ -78,6 +78,19 @@ TK_API int tk_row_sumsq(const void* x, int64_t x_row_stride, int64_t m, int64_t 
                  void* stream);
 
 /*
+ * The embedding gather of a decoder's first step with the row statistics of its output:
+ * out[r, :] = table[tokens[r], :] ([rows, hidden] contiguous, table [vocab, hidden] contiguous,
+ * tokens int64 on the device) and, if row_ssq_out is not NULL, row_ssq_out[(c / 32) * rows + r] =
+ * the sum of squares of out[r, c .. c+31] - the row_ssq_in of the first folded RMSNorm, so that
+ * tk_row_sumsq need not run. Replaces `x = self.embedding(tokens)` of the reference's decoder
+ * (benchmarks/bench_e2e.py:95,104; nn.Embedding without padding_idx / max_norm) plus the
+ * statistics pass of its first RMSNorm. A token outside [0, vocab) records device error 3
+ * (tk_device_error) and gives a zero row. hidden a multiple of 32; dtype in {F16, BF16}.
+ */
+TK_API int tk_embedding_rows(const int64_t* tokens, const void* table, int64_t vocab, int64_t hidden, void* out,
+                             float* row_ssq_out, int64_t rows, int dtype, void* stream);
+
+/*
  * Residual add fused with RMSNorm: s = x + residual (rounded to dtype), written
  * to residual_out; y = rmsnorm(s). The residual update of the reference decoder
  * block (benchmarks/bench_e2e.py:112-115) followed by its next norm

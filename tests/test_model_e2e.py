@@ -188,3 +188,37 @@ def test_folded_norm_statistics_follow_in_place_changes():
     with torch.no_grad():  # version counters exist outside inference mode
         ya, yb = a(tokens).float(), b(tokens).float()
     assert ((ya - yb).norm() / ya.norm()).item() < 5e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_embedding_rows_is_the_gather_with_row_statistics(dtype):
+    """tk_embedding_rows: the rows of nn.Embedding bit for bit, the per-32-column sums of squares of
+    tk_row_sumsq, and a token outside the table as device error 3 with a zero row; optimize() gives a
+    plain decoder's embedding this forward and its first folded block then skips its statistics."""
+    require_b200()
+    import tinker_b200
+    from tinker_b200 import _lib
+    from tinker_b200.kernels.gemm import embedding_rows, row_sumsq
+    from bench_model import TINY, build_model, make_tokens
+    g = torch.Generator(device="cuda").manual_seed(2)
+    table = torch.randn(1000, 256, device="cuda", generator=g).to(dtype)
+    ids = torch.randint(0, 1000, (3, 37), device="cuda", generator=g)
+    out, parts = embedding_rows(ids, table)
+    torch.cuda.synchronize()
+    assert torch.equal(out, table[ids])
+    np.testing.assert_allclose(np32(parts), np32(row_sumsq(out)), rtol=1e-6, atol=1e-6)
+    _lib.device_error(clear=True)
+    bad = ids.clone()
+    bad[1, 5] = 1000
+    out2, _ = embedding_rows(bad, table)
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 3
+    assert torch.count_nonzero(out2[1, 5]) == 0 and torch.equal(out2[0], out[0])
+    model = tinker_b200.optimize(build_model(TINY, seed=3).cuda(), dtype=dtype)
+    assert "forward" in model.embedding.__dict__
+    tokens = make_tokens(TINY, 2, 24, seed=4).cuda()
+    with torch.inference_mode():
+        n0 = _lib.launch_counter[0]
+        model(tokens)
+        assert _lib.launch_counter[0] - n0 == 5 * TINY.num_layers + 2  # embedding + blocks + final norm

@@ -182,7 +182,15 @@ def test_dataflow_check_accepts_lm_and_rejects_other_forwards():
                 x = layer(x)
             return torch.softmax(self.output(self.norm(x)), dim=-1)
 
-    for cls in (Scaled, Skip, Soft):
+    class InPlace(Scaled):
+        def forward(self, tokens):
+            x = self.embedding(tokens)
+            x.mul_(2.0)  # the same tensor goes on, with other values
+            for layer in self.layers:
+                x = layer(x)
+            return self.output(self.norm(x))
+
+    for cls in (Scaled, Skip, Soft, InPlace):
         w = cls(m)
         assert not _dataflow_is_lm(w, w.forward, *parts, "cpu"), cls.__name__
     # the stubs are gone again

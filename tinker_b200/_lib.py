@@ -66,6 +66,7 @@ SIGNATURES = {
     "tk_gate_up_swiglu": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_gate_up_swiglu_ex": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _EPI, _I, _P],
     "tk_row_sumsq": [_P, _I64, _I64, _I64, _P, _I, _P],
+    "tk_embedding_rows": [_P, _P, _I64, _I64, _P, _P, _I64, _I, _P],
     "tk_swiglu_ffn": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_swiglu_ffn_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P],
     "tk_kv_attention": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _I, _I,

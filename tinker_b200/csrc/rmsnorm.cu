@@ -301,8 +301,66 @@ __global__ void __launch_bounds__(256) row_sumsq_kernel(const void* __restrict__
   parts[static_cast<int64_t>(c) * m + r] = ss;
 }
 
+// out[r, c .. c+31] = table[tokens[r], c .. c+31] and parts[(c / 32) * m + r] = the chunk's sum of
+// squares: a model's embedding gather together with the row statistics its first folded RMSNorm
+// reads, one thread per (row, 32-column chunk), the 64-byte copies of a warp contiguous. A token
+// outside [0, vocab) records TK_DEVERR_TOKEN and gives a zero row.
+template <int DT>
+__global__ void __launch_bounds__(256) embedding_rows_kernel(const int64_t* __restrict__ tokens,
+                                                              const void* __restrict__ table, int64_t vocab,
+                                                              int64_t hidden, void* __restrict__ out, int64_t m,
+                                                              int chunks, float* __restrict__ parts) {
+  pdl_launch_dependents();
+  pdl_wait();  // the token ids may be written by an earlier kernel
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= m * chunks) return;
+  const int64_t r = t / chunks;
+  const int c = static_cast<int>(t - r * chunks);
+  using V = Vec<DT>;
+  const int64_t tok = __ldg(tokens + r);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + r * hidden + c * 32);
+  float ss = 0.f;
+  if (tok < 0 || tok >= vocab) {
+    if (c == 0) record_device_error(TK_DEVERR_TOKEN);
+#pragma unroll
+    for (int q = 0; q < 32 / V::N; ++q) dst[q] = make_uint4(0, 0, 0, 0);
+  } else {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(table) + tok * hidden + c * 32);
+#pragma unroll
+    for (int q = 0; q < 32 / V::N; ++q) {
+      const uint4 u = __ldg(src + q);
+      dst[q] = u;
+      float f[V::N];
+      V::to_f(u, f);
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+  }
+  if (parts) parts[static_cast<int64_t>(c) * m + r] = ss;
+}
+
 }  // namespace
 }  // namespace tk
+
+extern "C" int tk_embedding_rows(const int64_t* tokens, const void* table, int64_t vocab, int64_t hidden, void* out,
+                                 float* row_ssq_out, int64_t rows, int dtype, void* stream) {
+  using namespace tk;
+  if (!half_dtype(dtype)) return fail_invalid("embedding_rows: dtype must be F16 or BF16");
+  if (rows < 0 || vocab <= 0 || hidden <= 0 || hidden % 32 != 0)
+    return fail_invalid("embedding_rows: hidden must be a positive multiple of 32");
+  if (rows == 0) return TK_OK;
+  if (!tokens || !table || !out || !aligned16(table) || !aligned16(out))
+    return fail_invalid("embedding_rows: NULL or unaligned pointer");
+  const int chunks = static_cast<int>(hidden / 32);
+  const int64_t threads = rows * chunks;
+  const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TK_F16)
+    return launch_kernel(embedding_rows_kernel<TK_F16>, grid, block, 0, st, 1, "embedding_rows_kernel", tokens, table,
+                         vocab, hidden, out, rows, chunks, row_ssq_out);
+  return launch_kernel(embedding_rows_kernel<TK_BF16>, grid, block, 0, st, 1, "embedding_rows_kernel", tokens, table,
+                       vocab, hidden, out, rows, chunks, row_ssq_out);
+}
 
 extern "C" int tk_row_sumsq(const void* x, int64_t x_row_stride, int64_t m, int64_t k, float* parts, int dtype,
                             void* stream) {

@@ -91,6 +91,30 @@ def row_sumsq(x: torch.Tensor) -> torch.Tensor:
     return parts
 
 
+def embedding_rows(tokens: torch.Tensor, table: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``table[tokens]`` ([..., hidden], the gather of ``nn.Embedding`` without padding_idx / max_norm)
+    and its per-32-column row sums of squares (float32 [hidden/32, rows], the ``row_ssq_in`` of a
+    GEMM with the next RMSNorm folded in), in one launch. A token outside the table records device
+    error 3 (``tinker_b200._lib.device_error``) and gives a zero row."""
+    dev = _lib.require_cuda(tokens, table)
+    if table.dtype not in (torch.float16, torch.bfloat16) or table.dim() != 2 or not table.is_contiguous():
+        raise TypeError("embedding_rows: the table must be a contiguous float16 / bfloat16 [vocab, hidden] tensor")
+    vocab, hidden = table.shape
+    if hidden % 32:
+        raise ValueError("embedding_rows: hidden must be a multiple of 32")
+    ids = tokens.reshape(-1)
+    if ids.dtype != torch.int64 or not ids.is_contiguous():
+        ids = ids.to(torch.int64).contiguous()
+    rows = ids.numel()
+    out = torch.empty(*tokens.shape, hidden, dtype=table.dtype, device=table.device)
+    parts = torch.empty(hidden // 32, rows, dtype=torch.float32, device=table.device)
+    with call_ctx(dev):
+        _lib.check(_lib.lib().tk_embedding_rows(ids.data_ptr(), table.data_ptr(), vocab, hidden, out.data_ptr(),
+                                                parts.data_ptr(), rows, _lib.dtype_code(table.dtype),
+                                                _lib.stream_ptr(dev)), "tk_embedding_rows", 1)
+    return out, parts
+
+
 def linear(x: torch.Tensor, w0: torch.Tensor, w1: torch.Tensor | None = None, w2: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
            row_ssq_in: torch.Tensor | None = None, row_ssq_eps: float = 1e-6,

@@ -27,7 +27,7 @@ from tinker_b200 import _lib
 from tinker_b200.fusion import fuse_decoder_blocks, share_rope_tables
 from tinker_b200.kernels._common import stable_weights
 from tinker_b200.patch import patch_model
-from tinker_b200.stack import install_stack_forward
+from tinker_b200.stack import install_embedding_rows, install_stack_forward
 
 
 def optimize(
@@ -96,6 +96,8 @@ def optimize(
         n = fuse_decoder_blocks(model, verbose=verbose, fold_norms=fold_norms)
         if verbose:
             print(f"  [tinker] fused {n} decoder blocks (residual adds in the GEMM epilogues)")
+        if fold_norms and n:
+            install_embedding_rows(model, verbose=verbose)
         if stack_kernel and fold_norms and n:
             install_stack_forward(model, verbose=verbose)
 

@@ -32,7 +32,8 @@ import torch
 import torch.nn as nn
 
 from tinker_b200 import _lib
-from tinker_b200.fusion import _folded_forward, _folded_weights
+from tinker_b200.fusion import _folded_forward, _folded_weights, _version_of
+from tinker_b200.kernels.gemm import embedding_rows
 from tinker_b200.modules.attention import TinKerAttention
 from tinker_b200.modules.normalization import TinKerRMSNorm
 
@@ -112,6 +113,7 @@ def _dataflow_is_lm(model: nn.Module, orig_forward, emb, layers, norm, head, dev
     dt = emb.weight.dtype
     outs = [torch.randn(1, 4, hidden, device=device, generator=gen).to(dt) for _ in range(len(mods) - 1)]
     outs.append(torch.randn(1, 4, head.weight.shape[0], device=device, generator=gen).to(dt))
+    kept = [o.clone() for o in outs]  # an in-place change of a stub's output shows against these
     seen: list[list] = [[] for _ in mods]
     saved = []
     for i, m in enumerate(mods):
@@ -141,6 +143,8 @@ def _dataflow_is_lm(model: nn.Module, orig_forward, emb, layers, norm, head, dev
     for i in range(1, len(mods)):
         if inputs[i] is not outs[i - 1]:
             return False
+    if not all(torch.equal(o, k) for o, k in zip(outs, kept)):
+        return False
     return result is outs[-1]
 
 
@@ -233,6 +237,36 @@ def _stack_forward(self, tokens, *args, **kwargs):
         plan = plans[shape] = _StackPlan(self, parts, *shape)
     # the model's LM head (torch's GEMM: measured faster than this library's at 128 rows)
     return parts[3](plan.hidden_states(tokens))
+
+
+def _embedding_rows_forward(self, tokens: torch.Tensor) -> torch.Tensor:
+    out, ssq = embedding_rows(tokens, self.weight)
+    out._tinker_row_ssq = (ssq, _version_of(out))  # read by the first folded block
+    return out
+
+
+def install_embedding_rows(model: nn.Module, verbose: bool = False) -> bool:
+    """Give the model's ``nn.Embedding`` a forward that gathers with ``tk_embedding_rows``, which also
+    writes the row statistics of its output, so that the first folded block skips its row-statistics
+    launch. Only for a forward that is exactly head(norm(blocks(embedding(tokens)))) (checked with
+    stubs: an embedding output that the model scales or changes before the first block keeps the
+    plain gather) whose first block is a folded block. Returns whether it was installed."""
+    parts = _parts(model)
+    if parts is None:
+        return False
+    emb, layers, norm, head = parts
+    w = emb.weight
+    if (emb.padding_idx is not None or emb.max_norm is not None or "forward" in emb.__dict__ or not w.is_cuda
+            or w.dtype not in (torch.float16, torch.bfloat16) or not w.is_contiguous() or w.shape[1] % 32):
+        return False
+    if getattr(getattr(layers[0], "forward", None), "__func__", None) is not _folded_forward:
+        return False
+    if not _dataflow_is_lm(model, model.forward, emb, layers, norm, head, w.device):
+        return False
+    emb.forward = types.MethodType(_embedding_rows_forward, emb)
+    if verbose:
+        print("  [tinker] embedding gather with the first block's row statistics (one launch)")
+    return True
 
 
 def install_stack_forward(model: nn.Module, verbose: bool = False) -> bool:
