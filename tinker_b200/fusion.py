@@ -151,7 +151,8 @@ def _folded_forward(self, x: torch.Tensor, kv_cache=None, start_pos: int = 0,
         a = causal_attention(qkv[..., :hq], qkv[..., hq:hq + hkv], qkv[..., hq + hkv:], at.num_heads,
                              at.num_kv_heads, at.head_dim)
     ssq_h = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
-    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h, l2_prefetch=_ahead_weights(self) if hint else None)
+    h = linear(a, at.o_proj.weight, residual=x, row_ssq_out=ssq_h,
+               l2_prefetch=_ahead_weights(self) if hint else None)
     g = gate_up_swiglu(h, wg, wu, row_ssq_in=ssq_h, row_ssq_eps=n2.eps)
     ssq_y = torch.empty(H // 32, m, dtype=torch.float32, device=x.device)
     y = linear(g, ff.down_proj.weight, residual=h, row_ssq_out=ssq_y)
