@@ -9,10 +9,17 @@ the measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096
 FFN (gate|up GEMM with the SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at
 1024 -> 2816 and 2048 -> 5632; causal RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512,
 2048} x head_dim {64, 128} x heads 16/4, 16/16, 16/1; and the ~1B Llama-style decoder at batch
-{1, 16} x seq {128, 2048}. The comparison arm restates the reference's eager fallbacks in torch
-(`_rmsnorm_pytorch` tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
+{1, 16} x seq {128, 2048}. The eager comparison arm restates the reference's eager fallbacks in
+torch (`_rmsnorm_pytorch` tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
 tinker/modules/feed_forward.py:26-30 with `_swiglu_pytorch` fused_swiglu.py:57-58,
-`_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA.
+`_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA. The Triton arm runs the
+reference's own GPU path on the same inputs: its public kernel entries with Triton present
+(`fused_rmsnorm` fused_rmsnorm.py:70-74 -> the kernel of :12-52; `fused_swiglu` fused_swiglu.py:61-66
+-> :13-44, between two cuBLAS projections as feed_forward.py:26-30 calls it; `fused_attention`
+fused_attention.py:234-238 -> `_attention_triton` :195-231, the Triton RoPE and attention kernels of
+:19-154), imported from the reference package installed under
+`baseline/_ref`; without that package (or without Triton) the column is left out and the first line
+says why (`--no-triton` skips it).
 
 Timing: each call is captured 20+ times in a CUDA graph, rotating over enough copies of its
 inputs that one replay touches more than twice the 126 MB L2 (so HBM figures are not L2 hits),
@@ -23,14 +30,16 @@ Roofline denominators come from MEASURED_PEAKS.json (HBM copy GB/s, bf16 dense T
 from __future__ import annotations
 
 import argparse
+import importlib
 import json
 import math
 import os
+import sys
 
 import torch
 import torch.nn.functional as F
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 L2_BYTES = 126 * 1024 * 1024
 DTYPES = {"fp16": torch.float16, "bf16": torch.bfloat16}
 
@@ -103,9 +112,51 @@ def _ref_attention(q, k, v, cos, sin, hq, hkv, d):
     return out.transpose(1, 2).contiguous().view(B, S, hq * d)
 
 
+# ---------------------------------------------------------------- reference Triton arm
+
+class _RefTriton:
+    """The reference's kernel modules (tinker.kernels.fused_rmsnorm / fused_swiglu /
+    fused_attention) from its installed package, or ``None`` attributes and ``why``."""
+
+    def __init__(self, enabled: bool):
+        self.rms = self.swiglu = self.attn = None
+        self.why = "skipped (--no-triton)"
+        if not enabled:
+            return
+        path = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(path, "tinker", "kernels")):
+            self.why = "the reference package is not installed under baseline/_ref"
+            return
+        sys.path.insert(0, path)
+        try:
+            mods = [importlib.import_module("tinker.kernels." + n)
+                    for n in ("fused_rmsnorm", "fused_swiglu", "fused_attention")]
+        except Exception as e:  # the comparison arm is optional; ours is not
+            self.why = f"importing the reference kernels failed: {type(e).__name__}: {e}"
+            return
+        finally:
+            sys.path.remove(path)
+        if not all(getattr(m, "HAS_TRITON", False) for m in mods):
+            self.why = "Triton is not importable, so the reference takes its torch fallbacks"
+            return
+        self.rms, self.swiglu, self.attn = mods
+        self.why = None
+
+    def time_or_none(self, fns):
+        """Microseconds per call, or None when the arm is unavailable."""
+        return None if self.why else _time_graph(fns)
+
+
+def _with_triton(row: dict, key: str, tri_us, ours_us):
+    if tri_us is not None:
+        row[key] = round(tri_us, 2)
+        row["speedup_vs_triton"] = round(tri_us / ours_us, 2)
+    return row
+
+
 # ---------------------------------------------------------------- sweeps
 
-def sweep_rmsnorm(dtypes, peaks, emit):
+def sweep_rmsnorm(dtypes, peaks, emit, tri):
     from tinker_b200.kernels import fused_rmsnorm
     g = torch.Generator(device="cuda").manual_seed(0)
     for dt in dtypes:
@@ -117,15 +168,17 @@ def sweep_rmsnorm(dtypes, peaks, emit):
                 w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
                 ours = _time_graph([lambda x=x: fused_rmsnorm(x, w, 1e-6) for x in xs])
                 ref = _time_graph([lambda x=x: _ref_rmsnorm(x, w, 1e-6) for x in xs])
+                ref_tri = tri.time_or_none([lambda x=x: tri.rms.fused_rmsnorm(x, w, 1e-6) for x in xs])
                 gbs = nbytes / ours * 1e-3
-                emit({"kind": "rmsnorm", "case": f"rows {rows} x hidden {h}", "dtype": str(dt)[6:],
+                emit(_with_triton({"kind": "rmsnorm", "case": f"rows {rows} x hidden {h}", "dtype": str(dt)[6:],
                       "ours_us": round(ours, 2), "ref_eager_us": round(ref, 2), "speedup": round(ref / ours, 2),
                       "bound": "hbm", "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
-                      "peak": f"{peaks['hbm_gbs']} GB/s {peaks['note']}", "bytes": nbytes})
+                      "peak": f"{peaks['hbm_gbs']} GB/s {peaks['note']}", "bytes": nbytes},
+                     "ref_triton_us", ref_tri, ours))
                 del xs
 
 
-def sweep_ffn(dtypes, peaks, emit):
+def sweep_ffn(dtypes, peaks, emit, tri):
     from tinker_b200.kernels import swiglu_ffn
     g = torch.Generator(device="cuda").manual_seed(1)
     for dt in dtypes:
@@ -140,19 +193,22 @@ def sweep_ffn(dtypes, peaks, emit):
                 xs = [torch.randn(t, h, device="cuda", generator=g).to(dt) for _ in range(n)]
                 ours = _time_graph([lambda x=x: swiglu_ffn(x, wg, wu, wd) for x in xs])
                 ref = _time_graph([lambda x=x: _ref_ffn(x, wg, wu, wd) for x in xs])
+                ref_tri = tri.time_or_none(
+                    [lambda x=x: F.linear(tri.swiglu.fused_swiglu(F.linear(x, wg), F.linear(x, wu)), wd) for x in xs])
                 tf = flops / ours * 1e-6
                 gbs = nbytes / ours * 1e-3
                 bound = "hbm" if t <= 128 else "tensor"
                 frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["tflops"]
-                emit({"kind": "swiglu_ffn", "case": f"tokens {t}, {h} -> {f}", "dtype": str(dt)[6:],
+                emit(_with_triton({"kind": "swiglu_ffn", "case": f"tokens {t}, {h} -> {f}", "dtype": str(dt)[6:],
                       "ours_us": round(ours, 2), "ref_eager_us": round(ref, 2), "speedup": round(ref / ours, 2),
                       "bound": bound, "tflops": round(tf, 1), "gbs": round(gbs, 1), "frac": round(frac, 3),
                       "peak": (f"{peaks['hbm_gbs']} GB/s" if bound == "hbm" else f"{peaks['tflops']} TF/s")
-                      + f" {peaks['note']}", "flops": flops, "bytes": nbytes})
+                      + f" {peaks['note']}", "flops": flops, "bytes": nbytes},
+                     "ref_triton_us", ref_tri, ours))
                 del xs
 
 
-def sweep_attention(dtypes, peaks, emit):
+def sweep_attention(dtypes, peaks, emit, tri):
     from tinker_b200.kernels import causal_attention, fused_attention, precompute_rope_tables
     g = torch.Generator(device="cuda").manual_seed(2)
     for dt in dtypes:
@@ -170,14 +226,17 @@ def sweep_attention(dtypes, peaks, emit):
                         rope = _time_graph([lambda t=t: fused_attention(*t, cos, sin, hq, hkv, d) for t in qkv])
                         plain = _time_graph([lambda t=t: causal_attention(*t, hq, hkv, d) for t in qkv])
                         ref = _time_graph([lambda t=t: _ref_attention(*t, cos, sin, hq, hkv, d) for t in qkv])
+                        ref_tri = tri.time_or_none(
+                            [lambda t=t: tri.attn.fused_attention(*t, cos, sin, hq, hkv, d) for t in qkv])
                         tf_rope, tf_plain = flops / rope * 1e-6, flops / plain * 1e-6
-                        emit({"kind": "attention", "case": f"B {b} S {s} D {d} heads {hq}/{hkv}",
+                        emit(_with_triton({"kind": "attention", "case": f"B {b} S {s} D {d} heads {hq}/{hkv}",
                               "dtype": str(dt)[6:], "ours_rope_us": round(rope, 2), "ours_prerotated_us": round(plain, 2),
                               "ref_eager_us": round(ref, 2), "speedup": round(ref / rope, 2),
                               "bound": "latency" if s <= 128 else "tensor", "tflops_rope": round(tf_rope, 1),
                               "tflops_prerotated": round(tf_plain, 1), "frac_rope": round(tf_rope / peaks["tflops"], 3),
                               "frac_prerotated": round(tf_plain / peaks["tflops"], 3),
-                              "peak": f"{peaks['tflops']} TF/s {peaks['note']}", "flops": flops, "bytes": nbytes})
+                              "peak": f"{peaks['tflops']} TF/s {peaks['note']}", "flops": flops, "bytes": nbytes},
+                             "ref_triton_us", ref_tri, rope))
                         del qkv
 
 
@@ -269,6 +328,7 @@ def main(argv=None):
     ap.add_argument("--only", default="rmsnorm,ffn,attention,model1b")
     ap.add_argument("--dtypes", default="fp16,bf16")
     ap.add_argument("--case", default=None, help="run one configuration for a profiler (see run_case)")
+    ap.add_argument("--no-triton", action="store_true", help="leave out the reference's Triton arm")
     args = ap.parse_args(argv)
     torch.cuda.set_device(0)
     if args.case:
@@ -282,13 +342,16 @@ def main(argv=None):
         print(json.dumps(d), flush=True)
 
     kinds = args.only.split(",")
+    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "ffn", "attention")))
+    if tri.why and not args.no_triton:
+        emit({"kind": "note", "ref_triton": f"unavailable: {tri.why}"})
     with torch.inference_mode():
         if "rmsnorm" in kinds:
-            sweep_rmsnorm(dtypes, peaks, emit)
+            sweep_rmsnorm(dtypes, peaks, emit, tri)
         if "ffn" in kinds:
-            sweep_ffn(dtypes, peaks, emit)
+            sweep_ffn(dtypes, peaks, emit, tri)
         if "attention" in kinds:
-            sweep_attention(dtypes, peaks, emit)
+            sweep_attention(dtypes, peaks, emit, tri)
     if "model1b" in kinds:
         sweep_model1b(peaks, emit)
 

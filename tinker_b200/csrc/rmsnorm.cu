@@ -60,7 +60,10 @@ template <> __device__ __forceinline__ float round_dt<TK_BF16>(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
-template <int DT, int NV, int TPR, bool ADD>
+// WV: the weight has the row dtype and a 16-byte aligned base, so each thread loads its weight
+// vectors with the same 16-byte loads as the row, issued together with them (before the
+// reduction, off its critical path); otherwise the weights are read element by element after it.
+template <int DT, int NV, int TPR, bool ADD, bool WV>
 __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const void* __restrict__ x, int64_t xs,
                                                            const void* __restrict__ res, const void* __restrict__ w,
                                                            int wdt, void* y, int64_t ys, void* res_out,
@@ -77,7 +80,15 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const void* __restrict
   const int nvec = dim / E;
 
   float v[NV][E];
+  uint4 wr[WV ? NV : 1];
   float ss = 0.f;
+  if constexpr (WV) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = t + i * TPR;
+      if (active && c < nvec) wr[i] = reinterpret_cast<const uint4*>(w)[c];
+    }
+  }
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = t + i * TPR;
@@ -112,9 +123,15 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const void* __restrict
   for (int i = 0; i < NV; ++i) {
     const int c = t + i * TPR;
     if (c < nvec) {
-      float o[E];
+      float o[E], wf[E];
+      if constexpr (WV) {
+        V::to_f(wr[i], wf);
+      } else {
 #pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = v[i][e] * rrms * load_as_f32(w, static_cast<int64_t>(c) * E + e, wdt);
+        for (int e = 0; e < E; ++e) wf[e] = load_as_f32(w, static_cast<int64_t>(c) * E + e, wdt);
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[e] = v[i][e] * rrms * wf[e];
       reinterpret_cast<uint4*>(static_cast<char*>(y) + (row * ys) * (DT == TK_F32 ? 4 : 2))[c] = V::from_f(o);
     }
   }
@@ -165,6 +182,7 @@ int launch_rmsnorm(const void* x, int64_t xs, const void* res, const void* w, in
   const bool vec_ok = dim % E == 0 && (xs * es) % 16 == 0 && (ys * es) % 16 == 0 && aligned16(x) && aligned16(y) &&
                       (!ADD || (aligned16(res) && aligned16(res_out)));
   const int64_t nvec = dim / E;
+  const bool wv = wdt == DT && aligned16(w);
   DeviceInfo dev;
   if (int rc = current_device_info(&dev)) return rc;
   if (vec_ok && nvec <= 2048) {
@@ -172,8 +190,12 @@ int launch_rmsnorm(const void* x, int64_t xs, const void* res, const void* w, in
   {                                                                                                            \
     dim3 block(TPR, TPR >= 128 ? 1 : 128 / TPR);                                                               \
     dim3 grid(static_cast<unsigned>((rows + block.y - 1) / block.y));                                          \
-    return launch_kernel(rmsnorm_vec_kernel<DT, NV, TPR, ADD>, grid, block, 0, st, 1, "rmsnorm_vec_kernel", x, xs, \
-                         res, w, wdt, y, ys, res_out, rows, static_cast<int>(dim), eps);                      \
+    if (wv)                                                                                                    \
+      return launch_kernel(rmsnorm_vec_kernel<DT, NV, TPR, ADD, true>, grid, block, 0, st, 1,                  \
+                           "rmsnorm_vec_kernel", x, xs, res, w, wdt, y, ys, res_out, rows, static_cast<int>(dim), \
+                           eps);                                                                               \
+    return launch_kernel(rmsnorm_vec_kernel<DT, NV, TPR, ADD, false>, grid, block, 0, st, 1, "rmsnorm_vec_kernel", \
+                         x, xs, res, w, wdt, y, ys, res_out, rows, static_cast<int>(dim), eps);                \
   }
     if (rows < 4 * static_cast<int64_t>(dev.sm_count)) {
       // few rows: one row per block and one vector per thread, to spread a small
