@@ -1,15 +1,16 @@
 """Standalone kernel sweeps and the ~1B decoder, each against the reference's eager torch path
 on the same GPU.
 
-    python bench_sweep.py [--only rmsnorm,ffn,attention,model1b] [--dtypes fp16,bf16]
+    python bench_sweep.py [--only rmsnorm,ffn,attention,model268m,model1b] [--dtypes fp16,bf16]
 
 One JSON line per case on stdout. The cases are the standalone configurations the reference
 benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of
 the measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096}; the SwiGLU
 FFN (gate|up GEMM with the SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at
 1024 -> 2816 and 2048 -> 5632; causal RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512,
-2048} x head_dim {64, 128} x heads 16/4, 16/16, 16/1; and the ~1B Llama-style decoder at batch
-{1, 16} x seq {128, 2048}. The eager comparison arm restates the reference's eager fallbacks in
+2048} x head_dim {64, 128} x heads 16/4, 16/16, 16/1; the 268M decoder at batch 1 x seq 128 (the
+headline workload) against the reference's own optimize() on the same GPU; and the ~1B Llama-style
+decoder at batch {1, 16} x seq {128, 2048}. The eager comparison arm restates the reference's eager fallbacks in
 torch (`_rmsnorm_pytorch` tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
 tinker/modules/feed_forward.py:26-30 with `_swiglu_pytorch` fused_swiglu.py:57-58,
 `_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA. The Triton arm runs the
@@ -284,6 +285,49 @@ def sweep_model1b(peaks, emit):
         torch.cuda.empty_cache()
 
 
+def sweep_model268m(peaks, emit, tri):
+    """The headline workload, the 268M decoder at batch 1 x seq 128 in fp16 inside a CUDA graph, in three
+    arms on this GPU: this library's ``optimize``; the reference's own ``optimize`` (tinker/optimize.py:
+    27-117: ``patch_model`` onto its Triton modules, fp16, graph capture by ``_capture_cuda_graph`` :153-
+    171; ``compile=False``) on the same model; the unpatched fp16 model captured in a graph."""
+    import tinker_b200
+    from bench_model import LLAMA_268M, build_model, make_tokens
+    cfg = LLAMA_268M
+    b, s = 1, 128
+    reps = 200
+    tok = make_tokens(cfg, b, s, seed=1).cuda()
+    row = {"kind": "model_268m", "case": f"batch {b} x seq {s}", "dtype": "float16"}
+    base = build_model(cfg, seed=0).to("cuda", torch.float16).eval()
+    with torch.inference_mode():
+        row["ref_eager_graph_us"] = round(_time_graph([lambda: base(tok)], min_calls=reps), 1)
+    del base
+    torch.cuda.empty_cache()
+    m = tinker_b200.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, cuda_graph=True,
+                             graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size, graph_clone_output=False)
+    m._static_input.copy_(tok)
+    ours = _time_replays(m._graph, reps)
+    row["ours_us"] = round(ours, 1)
+    row["speedup_vs_eager_graph"] = round(row["ref_eager_graph_us"] / ours, 2)
+    if tri.why is None:
+        ref_opt = importlib.import_module("tinker.optimize")
+        rm = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, compile=False, cuda_graph=True,
+                              graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size)
+        if hasattr(rm, "_graph"):
+            rm._static_input.copy_(tok)
+            ref_us = _time_replays(rm._graph, reps)
+            row["ref_triton_graph_us"] = round(ref_us, 1)
+            row["speedup_vs_triton"] = round(ref_us / ours, 2)
+            # both graphs ran on the same tokens: the arms compute the same forward
+            row["max_abs_logits_vs_ours"] = float((rm._static_output.float() - m._static_output.float()).abs().max())
+        else:
+            row["ref_triton_graph_us"] = None
+            row["note"] = "the reference's graph capture failed, so its optimize returned the eager model"
+        del rm
+    emit(row)
+    del m
+    torch.cuda.empty_cache()
+
+
 def run_case(spec: str, reps: int = 3):
     """One configuration, eager, ``reps`` calls inside an NVTX range ``timed`` (for profilers):
     ``rmsnorm:ROWS,H`` | ``ffn:T,H,F`` | ``attention:B,S,D,HQ,HKV`` (pre-rotated kernel) |
@@ -325,7 +369,7 @@ def run_case(spec: str, reps: int = 3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="rmsnorm,ffn,attention,model1b")
+    ap.add_argument("--only", default="rmsnorm,ffn,attention,model268m,model1b")
     ap.add_argument("--dtypes", default="fp16,bf16")
     ap.add_argument("--case", default=None, help="run one configuration for a profiler (see run_case)")
     ap.add_argument("--no-triton", action="store_true", help="leave out the reference's Triton arm")
@@ -342,7 +386,7 @@ def main(argv=None):
         print(json.dumps(d), flush=True)
 
     kinds = args.only.split(",")
-    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "ffn", "attention")))
+    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "ffn", "attention", "model268m")))
     if tri.why and not args.no_triton:
         emit({"kind": "note", "ref_triton": f"unavailable: {tri.why}"})
     with torch.inference_mode():
@@ -352,6 +396,8 @@ def main(argv=None):
             sweep_ffn(dtypes, peaks, emit, tri)
         if "attention" in kinds:
             sweep_attention(dtypes, peaks, emit, tri)
+    if "model268m" in kinds:
+        sweep_model268m(peaks, emit, tri)
     if "model1b" in kinds:
         sweep_model1b(peaks, emit)
 
