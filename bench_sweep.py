@@ -254,6 +254,21 @@ def _time_replays(graph, reps: int) -> float:
     return e0.elapsed_time(e1) * 1e3 / reps
 
 
+def _time_calls(fn, reps: int) -> float:
+    """Microseconds per call of ``fn`` issued back to back (CUDA events around ``reps`` calls)."""
+    with torch.inference_mode():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
 def sweep_model1b(peaks, emit):
     import tinker_b200
     from bench_model import LLAMA_1B, build_model, make_tokens
@@ -289,7 +304,8 @@ def sweep_model268m(peaks, emit, tri):
     """The headline workload, the 268M decoder at batch 1 x seq 128 in fp16 inside a CUDA graph, in three
     arms on this GPU: this library's ``optimize``; the reference's own ``optimize`` (tinker/optimize.py:
     27-117: ``patch_model`` onto its Triton modules, fp16, graph capture by ``_capture_cuda_graph`` :153-
-    171; ``compile=False``) on the same model; the unpatched fp16 model captured in a graph."""
+    171; ``compile=False``), and the same with its default ``compile`` (torch.compile first); the unpatched
+    fp16 model captured in a graph."""
     import tinker_b200
     from bench_model import LLAMA_268M, build_model, make_tokens
     cfg = LLAMA_268M
@@ -323,6 +339,26 @@ def sweep_model268m(peaks, emit, tri):
             row["ref_triton_graph_us"] = None
             row["note"] = "the reference's graph capture failed, so its optimize returned the eager model"
         del rm
+        torch.cuda.empty_cache()
+        # the reference's default: compile=None means torch.compile(mode="reduce-overhead") when Triton
+        # is importable (tinker/optimize.py:77-85), then its graph capture of the compiled model
+        try:
+            rc = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, cuda_graph=True,
+                                  graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size)
+            if hasattr(rc, "_graph"):
+                rc._static_input.copy_(tok)
+                ref_c = _time_replays(rc._graph, reps)
+                row["ref_triton_compiled_note"] = "compiled model captured by the reference's graph wrapper"
+            else:
+                ref_c = _time_calls(lambda: rc(tok), reps)
+                row["ref_triton_compiled_note"] = ("the reference's graph capture of the compiled model failed, so "
+                                                   "its optimize returned the compiled model: timed per call")
+            row["ref_triton_compiled_us"] = round(ref_c, 1)
+            row["speedup_vs_triton_compiled"] = round(ref_c / ours, 2)
+            del rc
+        except Exception as e:  # a comparison arm; ours was measured above
+            msg = " ".join(str(e).split())
+            row["ref_triton_compiled_note"] = f"failed: {type(e).__name__}: {msg[:120]} ... {msg[-400:]}"
     emit(row)
     del m
     torch.cuda.empty_cache()
