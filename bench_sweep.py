@@ -1,26 +1,27 @@
 """Standalone kernel sweeps and the ~1B decoder, each against the reference's eager torch path
 on the same GPU.
 
-    python bench_sweep.py [--only rmsnorm,ffn,attention,model268m,model1b] [--dtypes fp16,bf16]
+    python bench_sweep.py [--only rmsnorm,swiglu,ffn,attention,model268m,model1b] [--dtypes fp16,bf16]
 
 One JSON line per case on stdout. The cases are the standalone configurations the reference
-benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of
-the measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096}; the SwiGLU
-FFN (gate|up GEMM with the SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at
-1024 -> 2816 and 2048 -> 5632; causal RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512,
-2048} x head_dim {64, 128} x heads 16/4, 16/16, 16/1; the 268M decoder at batch 1 x seq 128 (the
-headline workload) against the reference's own optimize() on the same GPU; and the ~1B Llama-style
-decoder at batch {1, 16} x seq {128, 2048}. The eager comparison arm restates the reference's eager fallbacks in
-torch (`_rmsnorm_pytorch` tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
+benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of the
+measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096}; the SwiGLU activation
+alone at the reference's shapes and at 4096 / 16384 tokens; the SwiGLU FFN (gate|up GEMM with the
+SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at 1024 -> 2816 and 2048 -> 5632; causal
+RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512, 2048} x head_dim {64, 128} x heads 16/4,
+16/16, 16/1; the 268M decoder at batch 1 x seq 128 (the headline workload) against the reference's
+own optimize() on the same GPU; and the ~1B Llama-style decoder at batch {1, 16} x seq {128, 2048}.
+The eager comparison arm restates the reference's eager fallbacks in torch (`_rmsnorm_pytorch`
+tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
 tinker/modules/feed_forward.py:26-30 with `_swiglu_pytorch` fused_swiglu.py:57-58,
 `_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA. The Triton arm runs the
 reference's own GPU path on the same inputs: its public kernel entries with Triton present
-(`fused_rmsnorm` fused_rmsnorm.py:70-74 -> the kernel of :12-52; `fused_swiglu` fused_swiglu.py:61-66
--> :13-44, between two cuBLAS projections as feed_forward.py:26-30 calls it; `fused_attention`
-fused_attention.py:234-238 -> `_attention_triton` :195-231, the Triton RoPE and attention kernels of
-:19-154), imported from the reference package installed under
-`baseline/_ref`; without that package (or without Triton) the column is left out and the first line
-says why (`--no-triton` skips it).
+(`fused_rmsnorm` fused_rmsnorm.py:70-74 -> the kernel of :12-52; `fused_swiglu`
+fused_swiglu.py:61-66 -> :13-44, between two cuBLAS projections as feed_forward.py:26-30 calls it;
+`fused_attention` fused_attention.py:234-238 -> `_attention_triton` :195-231, the Triton RoPE and
+attention kernels of :19-154), imported from the reference package installed under `baseline/_ref`;
+without that package (or without Triton) the column is left out and the first line says why
+(`--no-triton` skips it).
 
 Timing: each call is captured 20+ times in a CUDA graph, rotating over enough copies of its
 inputs that one replay touches more than twice the 126 MB L2 (so HBM figures are not L2 hits),
@@ -177,6 +178,32 @@ def sweep_rmsnorm(dtypes, peaks, emit, tri):
                       "peak": f"{peaks['hbm_gbs']} GB/s {peaks['note']}", "bytes": nbytes},
                      "ref_triton_us", ref_tri, ours))
                 del xs
+
+
+def sweep_swiglu(dtypes, peaks, emit, tri):
+    """The activation alone, ``silu(gate) * up`` on [tokens, F]: the reference's own benchmark shapes
+    (benchmarks/bench_swiglu.py:21-30: batch 1 and 4 x seq 128 at F 1376, 2816, 3584, 5504) plus 4096 and
+    16384 tokens, where it is HBM-bound (bytes = 3 x tokens x F x 2)."""
+    from tinker_b200.kernels import fused_swiglu
+    g = torch.Generator(device="cuda").manual_seed(4)
+    for dt in dtypes:
+        for t, f in [(t, f) for f in (1376, 2816, 3584, 5504) for t in (128, 512)] + \
+                    [(4096, 2816), (4096, 5504), (16384, 2816), (16384, 5504)]:
+            nbytes = 3 * t * f * 2
+            n = _copies(nbytes)
+            gu = [(torch.randn(t, f, device="cuda", generator=g).to(dt),
+                   torch.randn(t, f, device="cuda", generator=g).to(dt)) for _ in range(n)]
+            ours = _time_graph([lambda p=p: fused_swiglu(*p) for p in gu])
+            ref = _time_graph([lambda p=p: F.silu(p[0]) * p[1] for p in gu])
+            ref_tri = tri.time_or_none([lambda p=p: tri.swiglu.fused_swiglu(*p) for p in gu])
+            gbs = nbytes / ours * 1e-3
+            emit(_with_triton({"kind": "swiglu", "case": f"tokens {t} x F {f}", "dtype": str(dt)[6:],
+                               "ours_us": round(ours, 2), "ref_eager_us": round(ref, 2),
+                               "speedup": round(ref / ours, 2), "bound": "hbm", "gbs": round(gbs, 1),
+                               "frac": round(gbs / peaks["hbm_gbs"], 3),
+                               "peak": f"{peaks['hbm_gbs']} GB/s {peaks['note']}", "bytes": nbytes},
+                              "ref_triton_us", ref_tri, ours))
+            del gu
 
 
 def sweep_ffn(dtypes, peaks, emit, tri):
@@ -405,7 +432,7 @@ def run_case(spec: str, reps: int = 3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="rmsnorm,ffn,attention,model268m,model1b")
+    ap.add_argument("--only", default="rmsnorm,swiglu,ffn,attention,model268m,model1b")
     ap.add_argument("--dtypes", default="fp16,bf16")
     ap.add_argument("--case", default=None, help="run one configuration for a profiler (see run_case)")
     ap.add_argument("--no-triton", action="store_true", help="leave out the reference's Triton arm")
@@ -422,12 +449,14 @@ def main(argv=None):
         print(json.dumps(d), flush=True)
 
     kinds = args.only.split(",")
-    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "ffn", "attention", "model268m")))
+    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "swiglu", "ffn", "attention", "model268m")))
     if tri.why and not args.no_triton:
         emit({"kind": "note", "ref_triton": f"unavailable: {tri.why}"})
     with torch.inference_mode():
         if "rmsnorm" in kinds:
             sweep_rmsnorm(dtypes, peaks, emit, tri)
+        if "swiglu" in kinds:
+            sweep_swiglu(dtypes, peaks, emit, tri)
         if "ffn" in kinds:
             sweep_ffn(dtypes, peaks, emit, tri)
         if "attention" in kinds:

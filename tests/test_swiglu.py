@@ -48,6 +48,26 @@ def test_fused_swiglu_shape_assert_and_odd_sizes():
                                rtol=ulp(torch.float16), atol=1e-6)
 
 
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("rows, inter", [(4099, 2816), (1, 8), (37, 1376)])
+def test_fused_swiglu_contiguous_sizes_and_strided_rows(rows, inter, dt):
+    """Contiguous inputs run as one flat array of 16-byte vectors (four per thread from a few thousand
+    rows on, with a ragged last block at 4099 rows); gate and up taken as the two halves of one
+    [rows, 2F] tensor (row stride 2F) run the strided kernel. Both equal the oracle to one ulp."""
+    require_b200()
+    from tinker_b200.kernels.fused_swiglu import fused_swiglu
+    torch.manual_seed(7)
+    dtype = DTYPES[dt]
+    gate = torch.randn(rows, inter, device="cuda", dtype=dtype)
+    up = torch.randn(rows, inter, device="cuda", dtype=dtype)
+    ref = oracle.swiglu(np32(gate), np32(up), out_dtype=NP_NAME[dtype])
+    np.testing.assert_allclose(np32(fused_swiglu(gate, up)), ref, rtol=ulp(dtype), atol=1e-6)
+    both = torch.cat([gate, up], dim=1)
+    g2, u2 = both[:, :inter], both[:, inter:]
+    assert g2.stride(0) == 2 * inter
+    np.testing.assert_allclose(np32(fused_swiglu(g2, u2)), ref, rtol=ulp(dtype), atol=1e-6)
+
+
 def _ffn_ref(x, wg, wu, wd):
     xx = np32(x).astype(np.float64).reshape(-1, x.shape[-1])
     a = xx @ np32(wg).astype(np.float64).T

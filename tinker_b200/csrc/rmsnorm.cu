@@ -237,6 +237,14 @@ int rmsnorm_dispatch(const void* x, int64_t xs, const void* res, const void* w, 
 }
 
 // ---- SwiGLU activation ---------------------------------------------------------
+// silu(a) * b in fp32. For 16-bit rows (one rounding to 11 or 8 significant bits follows) the fast
+// exponential and division intrinsics are used; fp32 rows keep expf and the IEEE division.
+template <int DT>
+__device__ __forceinline__ float silu_mul(float a, float b) {
+  if constexpr (DT == TK_F32) return a / (1.0f + expf(-a)) * b;
+  else return __fdividef(a, 1.0f + __expf(-a)) * b;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(const void* __restrict__ g, int64_t gs,
                                                           const void* __restrict__ u, int64_t us, void* o, int64_t os,
@@ -254,8 +262,42 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(const void* __restrict_
     V::to_f(reinterpret_cast<const uint4*>(static_cast<const char*>(g) + r * gs * ES)[c], a);
     V::to_f(reinterpret_cast<const uint4*>(static_cast<const char*>(u) + r * us * ES)[c], b);
 #pragma unroll
-    for (int e = 0; e < E; ++e) out[e] = a[e] / (1.0f + expf(-a[e])) * b[e];
+    for (int e = 0; e < E; ++e) out[e] = silu_mul<DT>(a[e], b[e]);
     reinterpret_cast<uint4*>(static_cast<char*>(o) + r * os * ES)[c] = V::from_f(out);
+  }
+}
+
+// Contiguous gate, up and output: a flat array of 16-byte vectors. Each thread loads U vectors of
+// each input (a block covers 256 x U consecutive vectors, coalesced per step) before it computes,
+// so 2U loads are in flight per thread; no index division.
+template <int DT, int U>
+__global__ void __launch_bounds__(256) swiglu_flat_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                                                           uint4* __restrict__ o, int64_t total) {
+  using V = Vec<DT>;
+  constexpr int E = V::N;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (256 * U) + threadIdx.x;
+  uint4 ga[U], ua[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int64_t i = base + k * 256;
+    if (i < total) {
+      ga[k] = g[i];
+      ua[k] = u[i];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int64_t i = base + k * 256;
+    if (i < total) {
+      float a[E], b[E], out[E];
+      V::to_f(ga[k], a);
+      V::to_f(ua[k], b);
+#pragma unroll
+      for (int e = 0; e < E; ++e) out[e] = silu_mul<DT>(a[e], b[e]);
+      o[i] = V::from_f(out);
+    }
   }
 }
 
@@ -270,7 +312,7 @@ __global__ void __launch_bounds__(256) swiglu_scalar_kernel(const void* __restri
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / n, c = i - r * n;
     const float a = load_as_f32(g, r * gs + c, DT), b = load_as_f32(u, r * us + c, DT);
-    const float out = a / (1.0f + expf(-a)) * b;
+    const float out = silu_mul<DT>(a, b);
     if (DT == TK_F32) reinterpret_cast<float*>(o)[r * os + c] = out;
     else if (DT == TK_F16) reinterpret_cast<__half*>(o)[r * os + c] = __float2half_rn(out);
     else reinterpret_cast<__nv_bfloat16*>(o)[r * os + c] = __float2bfloat16_rn(out);
@@ -287,6 +329,20 @@ int launch_swiglu(const void* g, int64_t gs, const void* u, int64_t us, void* o,
   const int64_t cap = static_cast<int64_t>(dev.sm_count) * 8;
   const bool vec_ok = n % E == 0 && (gs * es) % 16 == 0 && (us * es) % 16 == 0 && (os * es) % 16 == 0 &&
                       aligned16(g) && aligned16(u) && aligned16(o);
+  if (vec_ok && gs == n && us == n && os == n) {
+    // four vectors per thread once that still leaves at least four blocks per SM; smaller problems
+    // take one vector per thread, to spread over more SMs
+    const int64_t total = rows * (n / E);
+    const int64_t blocks4 = (total + 256 * 4 - 1) / (256 * 4);
+    if (blocks4 > 0x7fffffffLL) return fail_invalid("swiglu: too many elements");
+    if (blocks4 >= 4 * static_cast<int64_t>(dev.sm_count))
+      return launch_kernel(swiglu_flat_kernel<DT, 4>, dim3(static_cast<unsigned>(blocks4)), dim3(256), 0, st, 1,
+                           "swiglu_flat_kernel", static_cast<const uint4*>(g), static_cast<const uint4*>(u),
+                           static_cast<uint4*>(o), total);
+    return launch_kernel(swiglu_flat_kernel<DT, 1>, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+                         st, 1, "swiglu_flat_kernel", static_cast<const uint4*>(g), static_cast<const uint4*>(u),
+                         static_cast<uint4*>(o), total);
+  }
   if (vec_ok) {
     const int64_t total = rows * (n / E);
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cap, (total + 255) / 256)));
