@@ -1,7 +1,8 @@
 """Standalone kernel sweeps and the ~1B decoder, each against the reference's eager torch path
 on the same GPU.
 
-    python bench_sweep.py [--only rmsnorm,swiglu,ffn,attention,model268m,model1b] [--dtypes fp16,bf16]
+    python bench_sweep.py [--only rmsnorm,swiglu,ffn,attention,model268m,modelqwen,model1b]
+                          [--dtypes fp16,bf16]
 
 One JSON line per case on stdout. The cases are the standalone configurations the reference
 benchmarks (benchmarks/bench_rmsnorm.py, bench_swiglu.py, bench_attention.py) at the sizes of the
@@ -9,9 +10,10 @@ measurement plan: RMSNorm rows {128, 4096, 65536} x hidden {1024, 2048, 4096}; t
 alone at the reference's shapes and at 4096 / 16384 tokens; the SwiGLU FFN (gate|up GEMM with the
 SwiGLU epilogue, then down) for tokens {128, 4096, 16384} at 1024 -> 2816 and 2048 -> 5632; causal
 RoPE + GQA attention for batch {1, 8, 32} x seq {128, 512, 2048} x head_dim {64, 128} x heads 16/4,
-16/16, 16/1; the 268M decoder at batch 1 x seq 128 (the headline workload) against the reference's
-own optimize() on the same GPU; and the ~1B Llama-style decoder at batch {1, 16} x seq {128, 2048}.
-The eager comparison arm restates the reference's eager fallbacks in torch (`_rmsnorm_pytorch`
+16/16, 16/1; the 268M decoder at batch 1 x seq 128 (the headline workload) and the
+Qwen2.5-0.5B-shaped decoder at batch 64 x seq 512 against the reference's own optimize() on the same
+GPU; and the ~1B Llama-style decoder at batch {1, 16} x seq {128, 2048}. The eager comparison arm
+restates the reference's eager fallbacks in torch (`_rmsnorm_pytorch`
 tinker/kernels/fused_rmsnorm.py:64-67, `down(silu(gate(x)) * up(x))` of
 tinker/modules/feed_forward.py:26-30 with `_swiglu_pytorch` fused_swiglu.py:57-58,
 `_attention_pytorch` fused_attention.py:176-192), run on cuBLAS / SDPA. The Triton arm runs the
@@ -117,11 +119,15 @@ def _ref_attention(q, k, v, cos, sin, hq, hkv, d):
 # ---------------------------------------------------------------- reference Triton arm
 
 class _RefTriton:
-    """The reference's kernel modules (tinker.kernels.fused_rmsnorm / fused_swiglu /
-    fused_attention) from its installed package, or ``None`` attributes and ``why``."""
+    """The reference's kernel modules (tinker.kernels.fused_rmsnorm / fused_swiglu / fused_attention)
+    and its ``tinker.optimize`` from its installed package, or ``None`` attributes and ``why``.
+
+    This repository's own ``tinker`` package (the import-name alias of tinker_b200) may already be in
+    ``sys.modules``; it is set aside while the reference is imported and put back afterwards, so the
+    reference modules held here and the alias seen by everything else stay distinct."""
 
     def __init__(self, enabled: bool):
-        self.rms = self.swiglu = self.attn = None
+        self.rms = self.swiglu = self.attn = self.opt = None
         self.why = "skipped (--no-triton)"
         if not enabled:
             return
@@ -129,19 +135,28 @@ class _RefTriton:
         if not os.path.isdir(os.path.join(path, "tinker", "kernels")):
             self.why = "the reference package is not installed under baseline/_ref"
             return
+        aside = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "tinker" or k.startswith("tinker.")}
         sys.path.insert(0, path)
         try:
             mods = [importlib.import_module("tinker.kernels." + n)
                     for n in ("fused_rmsnorm", "fused_swiglu", "fused_attention")]
+            opt = importlib.import_module("tinker.optimize")
         except Exception as e:  # the comparison arm is optional; ours is not
             self.why = f"importing the reference kernels failed: {type(e).__name__}: {e}"
             return
         finally:
             sys.path.remove(path)
+            for k in [k for k in sys.modules if k == "tinker" or k.startswith("tinker.")]:
+                del sys.modules[k]
+            sys.modules.update(aside)
+        if not all(os.path.abspath(m.__file__).startswith(os.path.abspath(path)) for m in mods + [opt]):
+            self.why = "the imported tinker modules are not the installed reference's"
+            return
         if not all(getattr(m, "HAS_TRITON", False) for m in mods):
             self.why = "Triton is not importable, so the reference takes its torch fallbacks"
             return
         self.rms, self.swiglu, self.attn = mods
+        self.opt = opt
         self.why = None
 
     def time_or_none(self, fns):
@@ -327,68 +342,80 @@ def sweep_model1b(peaks, emit):
         torch.cuda.empty_cache()
 
 
-def sweep_model268m(peaks, emit, tri):
-    """The headline workload, the 268M decoder at batch 1 x seq 128 in fp16 inside a CUDA graph, in three
-    arms on this GPU: this library's ``optimize``; the reference's own ``optimize`` (tinker/optimize.py:
-    27-117: ``patch_model`` onto its Triton modules, fp16, graph capture by ``_capture_cuda_graph`` :153-
-    171; ``compile=False``), and the same with its default ``compile`` (torch.compile first); the unpatched
-    fp16 model captured in a graph."""
+def _model_arms(emit, tri, kind, cfg, b, s, dtype, reps, compiled_arm):
+    """One decoder workload inside CUDA graphs, in up to four arms on this GPU: this library's
+    ``optimize``; the reference's own ``optimize`` (tinker/optimize.py:27-117: ``patch_model`` onto its
+    Triton modules, the dtype cast, graph capture by ``_capture_cuda_graph`` :153-171; ``compile=False``);
+    optionally the same with its default ``compile`` (torch.compile first); the unpatched model captured
+    in a graph. Graph replays are timed with CUDA events; every arm runs the same model and tokens."""
     import tinker_b200
-    from bench_model import LLAMA_268M, build_model, make_tokens
-    cfg = LLAMA_268M
-    b, s = 1, 128
-    reps = 200
+    from bench_model import build_model, make_tokens
     tok = make_tokens(cfg, b, s, seed=1).cuda()
-    row = {"kind": "model_268m", "case": f"batch {b} x seq {s}", "dtype": "float16"}
-    base = build_model(cfg, seed=0).to("cuda", torch.float16).eval()
+    row = {"kind": kind, "case": f"batch {b} x seq {s}", "dtype": str(dtype)[6:], "replays": reps}
+    base = build_model(cfg, seed=0).to("cuda", dtype).eval()
     with torch.inference_mode():
         row["ref_eager_graph_us"] = round(_time_graph([lambda: base(tok)], min_calls=reps), 1)
     del base
     torch.cuda.empty_cache()
-    m = tinker_b200.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, cuda_graph=True,
+    m = tinker_b200.optimize(build_model(cfg, seed=0).cuda(), dtype=dtype, cuda_graph=True,
                              graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size, graph_clone_output=False)
     m._static_input.copy_(tok)
     ours = _time_replays(m._graph, reps)
     row["ours_us"] = round(ours, 1)
     row["speedup_vs_eager_graph"] = round(row["ref_eager_graph_us"] / ours, 2)
     if tri.why is None:
-        ref_opt = importlib.import_module("tinker.optimize")
-        rm = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, compile=False, cuda_graph=True,
+        ref_opt = tri.opt
+        rm = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=dtype, compile=False, cuda_graph=True,
                               graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size)
         if hasattr(rm, "_graph"):
             rm._static_input.copy_(tok)
             ref_us = _time_replays(rm._graph, reps)
             row["ref_triton_graph_us"] = round(ref_us, 1)
             row["speedup_vs_triton"] = round(ref_us / ours, 2)
-            # both graphs ran on the same tokens: the arms compute the same forward
-            row["max_abs_logits_vs_ours"] = float((rm._static_output.float() - m._static_output.float()).abs().max())
+            # both graphs ran on the same tokens (first and last sequence compared): the same forward
+            row["max_abs_logits_vs_ours"] = max(
+                float((rm._static_output[i].float() - m._static_output[i].float()).abs().max()) for i in (0, b - 1))
         else:
             row["ref_triton_graph_us"] = None
             row["note"] = "the reference's graph capture failed, so its optimize returned the eager model"
         del rm
         torch.cuda.empty_cache()
-        # the reference's default: compile=None means torch.compile(mode="reduce-overhead") when Triton
-        # is importable (tinker/optimize.py:77-85), then its graph capture of the compiled model
-        try:
-            rc = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=torch.float16, cuda_graph=True,
-                                  graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size)
-            if hasattr(rc, "_graph"):
-                rc._static_input.copy_(tok)
-                ref_c = _time_replays(rc._graph, reps)
-                row["ref_triton_compiled_note"] = "compiled model captured by the reference's graph wrapper"
-            else:
-                ref_c = _time_calls(lambda: rc(tok), reps)
-                row["ref_triton_compiled_note"] = ("the reference's graph capture of the compiled model failed, so "
-                                                   "its optimize returned the compiled model: timed per call")
-            row["ref_triton_compiled_us"] = round(ref_c, 1)
-            row["speedup_vs_triton_compiled"] = round(ref_c / ours, 2)
-            del rc
-        except Exception as e:  # a comparison arm; ours was measured above
-            msg = " ".join(str(e).split())
-            row["ref_triton_compiled_note"] = f"failed: {type(e).__name__}: {msg[:120]} ... {msg[-400:]}"
+        if compiled_arm:
+            # the reference's default: compile=None means torch.compile(mode="reduce-overhead") when
+            # Triton is importable (tinker/optimize.py:77-85), then its graph capture of the compiled model
+            try:
+                rc = ref_opt.optimize(build_model(cfg, seed=0).cuda(), dtype=dtype, cuda_graph=True,
+                                      graph_input_shape=(b, s), graph_vocab_size=cfg.vocab_size)
+                if hasattr(rc, "_graph"):
+                    rc._static_input.copy_(tok)
+                    ref_c = _time_replays(rc._graph, reps)
+                    row["ref_triton_compiled_note"] = "compiled model captured by the reference's graph wrapper"
+                else:
+                    ref_c = _time_calls(lambda: rc(tok), reps)
+                    row["ref_triton_compiled_note"] = ("the reference's graph capture of the compiled model failed, "
+                                                       "so its optimize returned the compiled model: timed per call")
+                row["ref_triton_compiled_us"] = round(ref_c, 1)
+                row["speedup_vs_triton_compiled"] = round(ref_c / ours, 2)
+                del rc
+            except Exception as e:  # a comparison arm; ours was measured above
+                msg = " ".join(str(e).split())
+                row["ref_triton_compiled_note"] = f"failed: {type(e).__name__}: {msg[:120]} ... {msg[-400:]}"
     emit(row)
     del m
     torch.cuda.empty_cache()
+
+
+def sweep_model268m(peaks, emit, tri):
+    """The headline workload: the 268M decoder at batch 1 x seq 128, fp16, 200 replays per arm."""
+    from bench_model import LLAMA_268M
+    _model_arms(emit, tri, "model_268m", LLAMA_268M, 1, 128, torch.float16, 200, compiled_arm=True)
+
+
+def sweep_model_qwen(peaks, emit, tri):
+    """The batched workload: the Qwen2.5-0.5B-shaped decoder at batch 64 x seq 512, bf16, 3 replays per
+    arm (the reference's compiled path is left out: it fails in inductor, as at the 268M shape)."""
+    from bench_model import QWEN25_05B_SHAPED
+    _model_arms(emit, tri, "model_qwen_b64s512", QWEN25_05B_SHAPED, 64, 512, torch.bfloat16, 3, compiled_arm=False)
 
 
 def run_case(spec: str, reps: int = 3):
@@ -432,7 +459,7 @@ def run_case(spec: str, reps: int = 3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="rmsnorm,swiglu,ffn,attention,model268m,model1b")
+    ap.add_argument("--only", default="rmsnorm,swiglu,ffn,attention,model268m,modelqwen,model1b")
     ap.add_argument("--dtypes", default="fp16,bf16")
     ap.add_argument("--case", default=None, help="run one configuration for a profiler (see run_case)")
     ap.add_argument("--no-triton", action="store_true", help="leave out the reference's Triton arm")
@@ -449,7 +476,8 @@ def main(argv=None):
         print(json.dumps(d), flush=True)
 
     kinds = args.only.split(",")
-    tri = _RefTriton(not args.no_triton and any(k in kinds for k in ("rmsnorm", "swiglu", "ffn", "attention", "model268m")))
+    arms = ("rmsnorm", "swiglu", "ffn", "attention", "model268m", "modelqwen")
+    tri = _RefTriton(not args.no_triton and any(k in kinds for k in arms))
     if tri.why and not args.no_triton:
         emit({"kind": "note", "ref_triton": f"unavailable: {tri.why}"})
     with torch.inference_mode():
@@ -463,6 +491,8 @@ def main(argv=None):
             sweep_attention(dtypes, peaks, emit, tri)
     if "model268m" in kinds:
         sweep_model268m(peaks, emit, tri)
+    if "modelqwen" in kinds:
+        sweep_model_qwen(peaks, emit, tri)
     if "model1b" in kinds:
         sweep_model1b(peaks, emit)
 
